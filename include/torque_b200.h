@@ -1,0 +1,162 @@
+/*
+ * torque_b200.h — C ABI of libtorque_b200.so, the B200 (sm_100a) packed-KV
+ * decode path of torque-mlx.
+ *
+ * Every entry point takes plain device pointers and sizes, is ordered on the
+ * CUDA stream it is given (NULL = legacy default stream), allocates nothing,
+ * and returns 0 (TQ_OK) or a negative TQ_E_* status.  Argument errors are
+ * detected on the host before any launch.  No entry point keeps mutable global
+ * state, so separate host threads may call it on separate streams.
+ *
+ * Data formats (identical to the reference):
+ *   - a head vector of d = 64|128|256 scalars is rotated by Pi = D1 H D2 / sqrt(d)
+ *     (signs_left = D1, signs_right = D2; rotation.py:51-106),
+ *   - each rotated scalar becomes the index of the nearest centroid of a sorted
+ *     2^bits-entry fp32 codebook, ties to the lower index (quantization.py:120-125),
+ *   - indices are packed LSB-first, code i at bit i*bits of the vector, into
+ *     W = ceil(d*bits/32) uint32 words (quantization.py:156-201),
+ *   - a cache slab is [groups, capacity, W] words with groups = (seq, layer,
+ *     kv_head) flattened; the reference's [layers, kv_heads, seq, W] slab
+ *     (layout.py:34-35) is the batch-1 case.
+ *
+ * Reference citations are path:line inside the cbun/torque-mlx project.
+ */
+#ifndef TORQUE_B200_H
+#define TORQUE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* tq_stream_t; /* same type as cudaStream_t */
+
+enum tq_status {
+  TQ_OK = 0,
+  TQ_E_BITS = -1,      /* bits not in {2,3,4}           -> ValueError (quantization.py:16-18) */
+  TQ_E_HEAD_DIM = -2,  /* head_dim not in {64,128,256}  -> ValueError (rotation.py:14-16)     */
+  TQ_E_SHAPE = -3,     /* inconsistent sizes            -> ValueError (mlx_ops.py:351-357)   */
+  TQ_E_CUDA = -4,      /* a CUDA call failed            -> RuntimeError                      */
+  TQ_E_TIMEOUT = -5,   /* a bounded device wait gave up -> RuntimeError                      */
+  TQ_E_WORKSPACE = -6, /* workspace missing/too small   -> RuntimeError                      */
+  TQ_E_ARG = -7        /* null pointer / bad enum value -> ValueError                        */
+};
+
+enum tq_dtype { TQ_F32 = 0, TQ_F16 = 1, TQ_BF16 = 2 };
+
+enum tq_decode_mode {
+  TQ_DECODE_AUTO = 0,   /* tensor-core kernel when group_size >= 2, else exact */
+  TQ_DECODE_EXACT = 1,  /* fp32 CUDA-core kernel, centroids and query in fp32  */
+  TQ_DECODE_TENSOR = 2  /* mma.sync kernel, fp16 centroids/query/probabilities, fp32 accumulate */
+};
+
+/* ABI version of this header (bumped on any signature change). */
+int tq_abi_version(void);
+/* Human-readable text for a tq_status value. */
+const char* tq_status_string(int status);
+/* cudaError_t of the most recent TQ_E_CUDA on the calling thread. */
+int tq_last_cuda_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Primitives
+ * ------------------------------------------------------------------------- */
+
+/* y[r] = signs_second * H(signs_first * x[r]) / f32(sqrt(d)) for rows r; fp32 out.
+ * Forward rotation: first = signs_right, second = signs_left (RotationSpec.apply,
+ * rotation.py:88-94); inverse: first = signs_left, second = signs_right
+ * (RotationSpec.inverse, rotation.py:96-102).  Bit-exact with numpy. */
+int tq_rotate(const void* x, int x_dtype, float* y, int64_t rows, int head_dim,
+              const float* signs_first, const float* signs_second, tq_stream_t stream);
+
+/* codes[i] = argmin_k |x[i] - centroids[k]| (fp32, first index on ties).
+ * Replaces quantize (quantization.py:120-125) and the boundary-count
+ * quantize_mlx (quantization.py:139-148) of the MLX path. */
+int tq_quantize(const float* x, uint8_t* codes, int64_t n, const float* centroids, int bits,
+                tq_stream_t stream);
+
+/* words[r, :] = LSB-first packing of codes[r, 0:count] (pack_indices /
+ * pack_indices_batched, quantization.py:156-201).  words is [rows, ceil(count*bits/32)]. */
+int tq_pack(const uint8_t* codes, uint32_t* words, int64_t rows, int count, int bits,
+            tq_stream_t stream);
+
+/* codes[r, 0:count] from words[r, :] (unpack_indices, quantization.py:272-290). */
+int tq_unpack(const uint32_t* words, uint8_t* codes, int64_t rows, int count, int bits,
+              tq_stream_t stream);
+
+/* out[r, 0:d] = centroids[unpack(words[r])] — dequantize(unpack_indices(...))
+ * as used by TorqueKVCache.export_dequantized (cache.py:189-214). */
+int tq_dequantize_packed(const uint32_t* words, float* out, int64_t rows, int head_dim, int bits,
+                         const float* centroids, tq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Append: rotate + quantize + pack straight into a cache slab
+ * ------------------------------------------------------------------------- */
+
+/* For group g in [0, groups) and token t in [0, tokens):
+ *   pos = (start_pos ? start_pos[g / groups_per_seq] : 0) + pos_offset + t
+ *   k_slab[g*group_stride_words + pos*W + 0:W] = pack(quantize(Pi k[g, t, :], cent_k))
+ * and the same for v with cent_v when v != NULL.  k, v are contiguous
+ * [groups, tokens, head_dim] in x_dtype.  rotate = 0 skips Pi (input already
+ * rotated, as quantize_and_pack_rows_dual_metal expects).  Rows whose pos falls
+ * outside [0, capacity) are not written.
+ * Replaces TorqueKVCache.append's per-head loop (cache.py:78-96),
+ * TorqueKVCacheMLX._append_packed_tokens (cache_mlx.py:396-418) and
+ * quantize_and_pack_rows[_dual]_metal (mlx_ops.py:342-412). */
+int tq_append_kv(const void* k, const void* v, int x_dtype, int64_t groups, int tokens,
+                 int head_dim, int bits, const float* signs_left, const float* signs_right,
+                 int rotate, const float* cent_k, const float* cent_v, uint32_t* k_slab,
+                 uint32_t* v_slab, int64_t group_stride_words, int64_t capacity,
+                 const int32_t* start_pos, int groups_per_seq, int64_t pos_offset,
+                 tq_stream_t stream);
+
+/* start_pos[i] += delta for i in [0, n): advances device-resident sequence
+ * lengths after an append without a host round trip. */
+int tq_lengths_add(int32_t* lengths, int n, int delta, tq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode attention over packed codes
+ * ------------------------------------------------------------------------- */
+
+/* Bytes of workspace tq_decode needs for these sizes. */
+int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int64_t max_len,
+                             int mode, size_t* bytes);
+
+/* Grouped-query decode attention (q_len = 1) straight on packed codes.
+ *
+ * units = (seq, layer, kv_head) triples; unit u reads
+ *   k_slab/v_slab + u*unit_stride_words, tokens [0, n_u) with
+ *   n_u = (lengths ? lengths[u / units_per_seq] : 0) + len_offset, clamped to max_len.
+ * query is [units*group_size, head_dim] fp32 (query head h*G + g of unit u's
+ * layer and seq attends kv head h, cache_mlx.py:706-722).  rotate_query = 1
+ * applies Pi to the query first (cache.py:109); otherwise it is taken as rotated.
+ * out[u*G + g] = softmax(scale * q . K^T) V over the dequantized codes,
+ * optionally rotated back by Pi^T (inverse_rotate_output = 1, cache.py:131-134).
+ * lse (nullable) receives the natural-log sum-exp of the scaled scores
+ * (-inf for an empty sequence, whose output is 0 as in reference.py:40-41).
+ * Replaces TorqueKVCache.decode (cache.py:98-140), TorqueKVCacheMLX.decode_mlx
+ * (cache_mlx.py:173-234) and decode_packed_attention[_split_batched]
+ * (mlx_ops.py:571-595, 663-692). */
+int tq_decode(const float* query, int rotate_query, const float* signs_left,
+              const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
+              int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
+              int64_t len_offset, int64_t max_len, int64_t units, int group_size, int head_dim,
+              int bits, const float* cent_k, const float* cent_v, float scale, float* out,
+              float* lse, int inverse_rotate_output, int mode, void* workspace,
+              size_t workspace_bytes, tq_stream_t stream);
+
+/* Merge P normalised partial attentions over disjoint key sets (the sequence
+ * shards of a multi-GPU decode):
+ *   LSE = logsumexp_p lse[p, r];  out[r] = sum_p exp(lse[p, r] - LSE) outs[p, r, :]
+ * outs [parts, rows, head_dim], lses [parts, rows]; lse_out nullable;
+ * inverse_rotate applies Pi^T to the merged row.  New in this build: the
+ * reference runs on one device only (no counterpart). */
+int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, int head_dim,
+                 float* out, float* lse_out, int inverse_rotate, const float* signs_left,
+                 const float* signs_right, tq_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TORQUE_B200_H */

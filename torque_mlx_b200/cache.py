@@ -1,0 +1,406 @@
+"""Device-resident packed KV cache for B200 — the drop-in for the reference's
+``TorqueKVCache`` (src/torque_mlx/cache.py:36-227) that also covers the
+grouped-query / multi-token / append-then-attend surface of
+``TorqueKVCacheMLX`` (src/torque_mlx/cache_mlx.py:41-799) and adds a batch of
+independent sequences.
+
+Storage: two int32 slabs ``[batch, layers, kv_heads, capacity, W]`` holding
+the reference's packed uint32 words (``PackedKVLayout.tensor_shape`` with a
+leading batch axis), plus device-resident per-sequence lengths.  A unit
+``(seq, layer, kv_head)`` is one contiguous ``[capacity, W]`` run of words, so
+decode streams it front to back.  Every step runs in libtorque_b200.so:
+
+  append  -> tq_append_kv   (rotate + quantize + pack into the slab)
+             tq_lengths_add (advance the device lengths)
+  decode  -> tq_decode      (split-K packed attention + merge + Pi^T)
+
+Inputs may be numpy arrays (copied to the device; numpy comes back, like the
+reference) or torch tensors (CUDA tensors come back).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from math import sqrt
+
+import numpy as np
+import torch
+
+from . import _lib, _tensors, ops
+from .config import TorqueConfig
+from .layout import CacheMetadata, PackedKVLayout
+from .quantization import Codebook, build_gaussian_codebook, packed_words_for_head_dim
+from .rotation import RotationSpec
+
+_CAP_ALIGN = 128  # capacity granule (tokens); keeps every unit 16-byte aligned
+
+
+def _round_cap(n: int) -> int:
+    return max(_CAP_ALIGN, (n + _CAP_ALIGN - 1) // _CAP_ALIGN * _CAP_ALIGN)
+
+
+@dataclass(eq=False)
+class TorqueKVCache:
+    """Rotation-native packed KV cache on the GPU.
+
+    Same constructor fields and methods as the reference's numpy cache
+    (``config``, ``key_codebook``, ``value_codebook``; ``append``, ``decode``,
+    ``reset``, ``export_dequantized``, ``metadata``, ``sequence_length``) and
+    the MLX cache's knobs (``initial_capacity``, ``growth_factor``,
+    ``rotate_{keys,values}_on_append``, ``rotate_queries_on_decode``).
+
+    Extensions: ``batch_size`` independent sequences with their own lengths,
+    grouped-query decode (query heads = G x kv heads), multi-token appends,
+    ``decode_with_current`` and a ``decode_mode`` of ``"auto"`` (tensor cores
+    when G >= 2), ``"exact"`` (fp32 CUDA cores) or ``"tensor"``.
+    """
+
+    config: TorqueConfig = field(default_factory=TorqueConfig)
+    key_codebook: Codebook | None = None
+    value_codebook: Codebook | None = None
+    initial_capacity: int = 256
+    growth_factor: int = 2
+    batch_size: int = 1
+    decode_mode: str = "auto"
+    rotate_keys_on_append: bool = True
+    rotate_values_on_append: bool = True
+    rotate_queries_on_decode: bool = True
+
+    def __post_init__(self) -> None:
+        self.config.validate()
+        if self.initial_capacity <= 0:
+            raise ValueError("initial_capacity must be positive")
+        if self.growth_factor < 2:
+            raise ValueError("growth_factor must be at least 2")
+        if self.batch_size <= 0:
+            raise ValueError("batch_size must be positive")
+        ops.decode_mode_code(self.decode_mode)
+        cfg = self.config
+        # codebook seeds follow cache.py:48-55 (K: rotation_seed, V: rotation_seed + 1)
+        self.key_codebook = self.key_codebook or build_gaussian_codebook(cfg.bit_width, seed=cfg.rotation_seed)
+        self.value_codebook = self.value_codebook or build_gaussian_codebook(cfg.bit_width, seed=cfg.rotation_seed + 1)
+        if self.key_codebook.bit_width != cfg.bit_width or self.value_codebook.bit_width != cfg.bit_width:
+            raise ValueError("codebook bit width does not match the config")
+        self.rotation = RotationSpec.from_seed(head_dim=cfg.head_dim, seed=cfg.rotation_seed)
+        self._layout: PackedKVLayout = cfg.layout
+        self._W = packed_words_for_head_dim(cfg.head_dim, cfg.bit_width)
+        self._dev = _tensors.device()
+        self._ck = _tensors.to_cuda(self.key_codebook.centroids, torch.float32)
+        self._cv = _tensors.to_cuda(self.value_codebook.centroids, torch.float32)
+        self._signs = self.rotation.device_signs()
+        self._cap = _round_cap(self.initial_capacity)
+        shape = (self.batch_size, cfg.num_layers, cfg.kv_heads, self._cap, self._W)
+        self._k = torch.zeros(shape, dtype=torch.int32, device=self._dev)
+        self._v = torch.zeros(shape, dtype=torch.int32, device=self._dev)
+        self._len_dev = torch.zeros((self.batch_size,), dtype=torch.int32, device=self._dev)
+        self._len_host = np.zeros((self.batch_size,), dtype=np.int64)
+        self._ws = ops.Workspace()
+
+    # ------------------------------------------------------------------ info
+    @property
+    def sequence_length(self) -> int:
+        """Tokens held (the longest sequence when ``batch_size`` > 1)."""
+        return int(self._len_host.max())
+
+    @property
+    def lengths(self) -> np.ndarray:
+        return self._len_host.copy()
+
+    @property
+    def offset(self) -> int:
+        return self.sequence_length
+
+    @property
+    def capacity(self) -> int:
+        return self._cap
+
+    @property
+    def metadata(self) -> CacheMetadata:
+        cfg = self.config
+        return CacheMetadata(variant_id=cfg.variant_id, bit_width=cfg.bit_width, head_dim=cfg.head_dim,
+                             num_layers=cfg.num_layers, kv_heads=cfg.kv_heads,
+                             rotation_mode=cfg.rotation_mode.value, fused_weights=cfg.fused_weights,
+                             codebook_name=self.key_codebook.name)
+
+    @property
+    def key_slab(self) -> torch.Tensor:
+        """``[batch, layers, kv_heads, capacity, W]`` words (int32 storage)."""
+        return self._k
+
+    @property
+    def value_slab(self) -> torch.Tensor:
+        return self._v
+
+    @property
+    def device_lengths(self) -> torch.Tensor:
+        return self._len_dev
+
+    def packed_words(self) -> tuple[np.ndarray, np.ndarray]:
+        """Host copy of the packed words, reference layout ``[layers, kv_heads,
+        seq, W]`` (batch 1) or ``[batch, layers, kv_heads, seq, W]``."""
+        n = self.sequence_length
+        k = ops.as_numpy_words(self._k[..., :n, :])
+        v = ops.as_numpy_words(self._v[..., :n, :])
+        return (k[0], v[0]) if self.batch_size == 1 else (k, v)
+
+    # --------------------------------------------------------------- storage
+    def _ensure_capacity(self, needed: int) -> None:
+        if needed <= self._cap:
+            return
+        cap = self._cap
+        while cap < needed:
+            cap *= self.growth_factor
+        cap = _round_cap(cap)
+        shape = (self.batch_size, self.config.num_layers, self.config.kv_heads, cap, self._W)
+        nk = torch.zeros(shape, dtype=torch.int32, device=self._dev)
+        nv = torch.zeros(shape, dtype=torch.int32, device=self._dev)
+        n = self.sequence_length
+        nk[..., :n, :].copy_(self._k[..., :n, :])
+        nv[..., :n, :].copy_(self._v[..., :n, :])
+        self._k, self._v, self._cap = nk, nv, cap
+
+    def reset(self) -> None:
+        self._len_dev.zero_()
+        self._len_host[:] = 0
+
+    # ---------------------------------------------------------------- shapes
+    def _norm_kv(self, x, label: str) -> torch.Tensor:
+        """-> contiguous ``[batch, layers, kv_heads, T, d]`` on the device
+        (shape rules of cache.py:216-227 and cache_mlx.py:474-498)."""
+        cfg = self.config
+        L, H, d, B = cfg.num_layers, cfg.kv_heads, cfg.head_dim, self.batch_size
+        t = _tensors.to_cuda(x, torch.float32, keep_half=True)
+        s = tuple(t.shape)
+        if B == 1:
+            if s == (d,):
+                if (L, H) != (1, 1):
+                    raise ValueError(f"{label} shape {s} only valid for 1 layer / 1 head")
+                return t.reshape(1, 1, 1, 1, d)
+            if s == (H, d):
+                if L != 1:
+                    raise ValueError(f"{label} shape {s} only valid for 1 layer")
+                return t.reshape(1, 1, H, 1, d)
+            if s == (L, H, d):
+                return t.reshape(1, L, H, 1, d)
+            if len(s) == 3 and L == 1 and s[0] == H and s[2] == d:
+                return t.reshape(1, 1, H, s[1], d)
+            if len(s) == 4 and s[0] == L and s[1] == H and s[3] == d:
+                return t.reshape(1, L, H, s[2], d)
+            raise ValueError(f"{label} must have shape ({L}, {H}, seq_len, {d}) or a compatible single-token "
+                             f"form, got {s}")
+        if s == (B, L, H, d):
+            return t.reshape(B, L, H, 1, d)
+        if len(s) == 5 and s[:3] == (B, L, H) and s[4] == d:
+            return t
+        if L == 1 and len(s) == 3 and s == (B, H, d):
+            return t.reshape(B, 1, H, 1, d)
+        raise ValueError(f"{label} must have shape ({B}, {L}, {H}, seq_len, {d}) or ({B}, {L}, {H}, {d}), got {s}")
+
+    def _norm_query(self, x) -> tuple[torch.Tensor, int, tuple[int, ...]]:
+        """-> ([batch*layers*Hq, d] fp32, Hq, output shape)."""
+        cfg = self.config
+        L, H, d, B = cfg.num_layers, cfg.kv_heads, cfg.head_dim, self.batch_size
+        t = _tensors.to_cuda(x, torch.float32)
+        s = tuple(t.shape)
+        if B == 1:
+            if s == (d,):
+                if (L, H) != (1, 1):
+                    raise ValueError(f"query shape {s} only valid for 1 layer / 1 head")
+                hq, out_shape = 1, (d,)
+            elif len(s) == 2 and s[1] == d and L == 1:
+                hq, out_shape = s[0], s
+            elif len(s) == 3 and s[0] == L and s[2] == d:
+                hq = s[1]
+                out_shape = (hq, d) if L == 1 and hq != 1 else s
+                if L == 1 and hq == 1:
+                    out_shape = (d,)
+            else:
+                raise ValueError(f"query must have shape ({L}, query_heads, {d}) or a compatible 1-layer form, "
+                                 f"got {s}")
+        else:
+            if len(s) == 4 and s[0] == B and s[1] == L and s[3] == d:
+                hq, out_shape = s[2], s
+            elif L == 1 and len(s) == 3 and s[0] == B and s[2] == d:
+                hq, out_shape = s[1], s
+            else:
+                raise ValueError(f"query must have shape ({B}, {L}, query_heads, {d}), got {s}")
+        if hq % H != 0:
+            raise ValueError(f"query head count {hq} must be divisible by kv_heads {H}")
+        if hq // H > 16:
+            raise ValueError(f"query group size {hq // H} exceeds 16")
+        return t.reshape(B * L * hq, d).contiguous(), hq, out_shape
+
+    # ----------------------------------------------------------------- append
+    def _launch_append(self, k: torch.Tensor | None, v: torch.Tensor | None, *, groups: int, tokens: int,
+                       k_slab: torch.Tensor, v_slab: torch.Tensor, start: torch.Tensor, groups_per_seq: int,
+                       rotate: bool) -> None:
+        lib = _lib.load()
+        cfg = self.config
+        sl, sr = self._signs
+        first = k if k is not None else v
+        _lib.check(lib.tq_append_kv(
+            first.data_ptr(), v.data_ptr() if (k is not None and v is not None) else None,
+            _lib.dtype_code(first.dtype), groups, tokens, cfg.head_dim, cfg.bit_width, sl.data_ptr(), sr.data_ptr(),
+            int(rotate), (self._ck if k is not None else self._cv).data_ptr(), self._cv.data_ptr(),
+            (k_slab if k is not None else v_slab).data_ptr(), v_slab.data_ptr(), self._cap * self._W, self._cap,
+            start.data_ptr(), groups_per_seq, 0, _lib.stream_ptr()), "append")
+
+    def _write(self, keys: torch.Tensor, values: torch.Tensor, *, seq: int | None = None) -> int:
+        """Pack ``[B', L, H, T, d]`` rows at each sequence's current length
+        without advancing it; returns T."""
+        cfg = self.config
+        if keys.shape != values.shape:
+            raise ValueError(f"key/value shapes must match, got {tuple(keys.shape)} and {tuple(values.shape)}")
+        if values.dtype != keys.dtype:
+            values = values.to(keys.dtype)
+        T = int(keys.shape[3])
+        if T == 0:
+            return 0
+        if seq is None:
+            need = int(self._len_host.max()) + T
+        else:
+            need = int(self._len_host[seq]) + T
+        self._ensure_capacity(need)
+        groups = int(keys.shape[0]) * cfg.num_layers * cfg.kv_heads
+        gps = cfg.num_layers * cfg.kv_heads
+        if seq is None:
+            ks, vs, start = self._k, self._v, self._len_dev
+        else:
+            ks, vs, start = self._k[seq], self._v[seq], self._len_dev[seq:seq + 1]
+        k = keys.reshape(groups, T, cfg.head_dim).contiguous()
+        v = values.reshape(groups, T, cfg.head_dim).contiguous()
+        if self.rotate_keys_on_append == self.rotate_values_on_append:
+            self._launch_append(k, v, groups=groups, tokens=T, k_slab=ks, v_slab=vs, start=start,
+                                groups_per_seq=gps, rotate=self.rotate_keys_on_append)
+        else:
+            self._launch_append(k, None, groups=groups, tokens=T, k_slab=ks, v_slab=vs, start=start,
+                                groups_per_seq=gps, rotate=self.rotate_keys_on_append)
+            self._launch_append(None, v, groups=groups, tokens=T, k_slab=ks, v_slab=vs, start=start,
+                                groups_per_seq=gps, rotate=self.rotate_values_on_append)
+        return T
+
+    def _advance(self, T: int, seq: int | None = None) -> None:
+        lib = _lib.load()
+        if seq is None:
+            _lib.check(lib.tq_lengths_add(self._len_dev.data_ptr(), self.batch_size, T, _lib.stream_ptr()),
+                       "lengths")
+            self._len_host += T
+        else:
+            _lib.check(lib.tq_lengths_add(self._len_dev[seq:seq + 1].data_ptr(), 1, T, _lib.stream_ptr()),
+                       "lengths")
+            self._len_host[seq] += T
+
+    def append(self, *, key, value) -> None:
+        """Append one step (``[layers, kv_heads, d]`` and the reference's short
+        forms) or T tokens (``[layers, kv_heads, T, d]``) to every sequence
+        (cache.py:78-96, cache_mlx.py:151-171)."""
+        k = self._norm_kv(key, "key")
+        v = self._norm_kv(value, "value")
+        if k.shape[:4] != v.shape[:4]:
+            raise ValueError(f"key/value sequence dimensions must match, got {tuple(k.shape)} and {tuple(v.shape)}")
+        T = self._write(k, v)
+        if T:
+            self._advance(T)
+
+    append_many = append
+    append_many_mlx = append
+
+    def append_sequence(self, seq: int, *, key, value) -> None:
+        """Append ``[layers, kv_heads, T, d]`` tokens to sequence ``seq`` only
+        (ragged prefill of a batch)."""
+        if not 0 <= seq < self.batch_size:
+            raise ValueError(f"sequence index {seq} out of range")
+        cfg = self.config
+        t = _tensors.to_cuda(key, torch.float32, keep_half=True)
+        u = _tensors.to_cuda(value, torch.float32, keep_half=True)
+        want = (cfg.num_layers, cfg.kv_heads)
+        if t.dim() != 4 or tuple(t.shape[:2]) != want or t.shape[3] != cfg.head_dim or t.shape != u.shape:
+            raise ValueError(f"key/value must have shape ({want[0]}, {want[1]}, T, {cfg.head_dim})")
+        T = self._write(t.unsqueeze(0), u.unsqueeze(0), seq=seq)
+        if T:
+            self._advance(T, seq)
+
+    # ----------------------------------------------------------------- decode
+    def _decode(self, q: torch.Tensor, hq: int, *, extra: int, return_lse: bool):
+        cfg = self.config
+        G = hq // cfg.kv_heads
+        units = self.batch_size * cfg.num_layers * cfg.kv_heads
+        out = torch.empty_like(q)
+        lse = torch.empty((q.shape[0],), dtype=torch.float32, device=q.device) if return_lse else None
+        ops.decode_raw(query=q, k_slab=self._k, v_slab=self._v, unit_stride=self._cap * self._W,
+                       lengths=self._len_dev, units_per_seq=cfg.num_layers * cfg.kv_heads, len_offset=extra,
+                       max_len=min(self._cap, self.sequence_length + extra), units=units, group_size=G,
+                       head_dim=cfg.head_dim, bits=cfg.bit_width, cent_k=self._ck, cent_v=self._cv, out=out, lse=lse,
+                       rotate_query=self.rotate_queries_on_decode, inverse_rotate=not cfg.fused_weights,
+                       signs=self._signs, scale=1.0 / sqrt(cfg.head_dim), mode=self.decode_mode, workspace=self._ws)
+        return out, lse
+
+    def decode(self, *, query, return_lse: bool = False):
+        """Decode attention for one query step (cache.py:98-140,
+        cache_mlx.py:173-234).  ``query`` is ``[layers, Hq, d]`` (or the
+        reference's 1-layer short forms; ``[batch, layers, Hq, d]`` for a
+        batch); Hq = G x kv_heads.  Returns the same shape; with
+        ``return_lse`` also the natural-log sum-exp per query row."""
+        np_out = _tensors.is_numpy(query)
+        q, hq, out_shape = self._norm_query(query)
+        out, lse = self._decode(q, hq, extra=0, return_lse=return_lse)
+        res = _tensors.out(out.reshape(out_shape), np_out)
+        if return_lse:
+            lse_shape = out_shape[:-1] if len(out_shape) > 1 else ()
+            return res, _tensors.out(lse.reshape(lse_shape), np_out)
+        return res
+
+    decode_mlx = decode
+
+    def decode_with_current(self, *, query, key, value):
+        """Attend the cache plus one current token that is not yet appended
+        (cache_mlx.py:236-302): the token is packed at each sequence's next
+        position and attended, but the lengths do not advance, so a later
+        ``append`` of the same token gives the same cache."""
+        np_out = _tensors.is_numpy(query)
+        q, hq, out_shape = self._norm_query(query)
+        k = self._norm_kv(key, "key")
+        v = self._norm_kv(value, "value")
+        if k.shape[3] != 1 or v.shape[3] != 1:
+            raise ValueError("decode_with_current expects a single current token for key/value")
+        self._write(k, v)
+        out, _ = self._decode(q, hq, extra=1, return_lse=False)
+        return _tensors.out(out.reshape(out_shape), np_out)
+
+    decode_mlx_with_current = decode_with_current
+
+    # ------------------------------------------------------------------ misc
+    def export_dequantized(self) -> tuple[np.ndarray, np.ndarray]:
+        """Dequantized rotated contents ``[layers, kv_heads, seq, d]`` (or with
+        a leading batch axis) for tests and benchmarks (cache.py:189-214).
+        Positions past a shorter sequence's length are zero."""
+        cfg = self.config
+        n = self.sequence_length
+        keys = ops.dequantize_packed(self._k[..., :n, :].contiguous(), self._ck, bit_width=cfg.bit_width,
+                                     head_dim=cfg.head_dim)
+        values = ops.dequantize_packed(self._v[..., :n, :].contiguous(), self._cv, bit_width=cfg.bit_width,
+                                       head_dim=cfg.head_dim)
+        pos = torch.arange(n, device=self._dev)
+        valid = (pos[None, :] < self._len_dev[:, None].to(torch.int64)).reshape(self.batch_size, 1, 1, n, 1)
+        keys = (keys * valid).cpu().numpy()
+        values = (values * valid).cpu().numpy()
+        return (keys[0], values[0]) if self.batch_size == 1 else (keys, values)
+
+    def make_mask(self, N: int, *, window_size: int | None = None, return_array: bool = False):
+        """Attention mask helper of the MLX-LM cache protocol (cache_mlx.py:317-334)."""
+        if N == 1:
+            return None
+        if not return_array and (window_size is None or N <= window_size):
+            return "causal"
+        offset = self.offset
+        rinds = torch.arange(offset + N, device=self._dev)
+        linds = torch.arange(offset, offset + N, device=self._dev) if offset else rinds
+        mask = linds[:, None] >= rinds[None]
+        if window_size is not None:
+            mask = mask & (linds[:, None] < rinds[None] + window_size)
+        return mask
+
+
+# MLX-named alias for drop-in use of the grouped-query cache surface.
+TorqueKVCacheMLX = TorqueKVCache
+TorqueKVCacheB200 = TorqueKVCache

@@ -1,0 +1,118 @@
+// Shared device helpers for the packed-KV kernels (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/torque_b200.h"
+
+namespace tq {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// host-side status plumbing
+// ---------------------------------------------------------------------------
+void set_last_cuda_error(cudaError_t e);
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return TQ_E_CUDA;
+  }
+  return TQ_OK;
+}
+
+inline bool valid_bits(int b) { return b == 2 || b == 3 || b == 4; }
+inline bool valid_head_dim(int d) { return d == 64 || d == 128 || d == 256; }
+inline int words_for(int count, int bits) { return (count * bits + 31) / 32; }
+
+// f32(sqrt(d)) exactly as numpy rounds it (a C++ double literal converted to
+// float rounds to nearest, like np.float32(math.sqrt(d))).
+template <int D> struct SqrtD;
+template <> struct SqrtD<64>  { static constexpr float v = 8.0f; };
+template <> struct SqrtD<128> { static constexpr float v = (float)11.313708498984761; };
+template <> struct SqrtD<256> { static constexpr float v = 16.0f; };
+
+// ---------------------------------------------------------------------------
+// element loads
+// ---------------------------------------------------------------------------
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// ---------------------------------------------------------------------------
+// Walsh-Hadamard butterfly network across one warp.
+//
+// A d-vector lives in a warp as v[j] = x[j*32 + lane], j < d/32.  Stages run
+// in the order span = 1, 2, 4, ..., d/2 and each maps the pair
+// (x[i], x[i+span]) (bit `span` of i clear) to (a + b, a - b) in fp32, which
+// is the exact operation sequence of the reference's numpy transform, so the
+// result is bit-identical.  Spans < 32 cross lanes (shuffle), larger spans
+// pair registers of the same lane.
+// ---------------------------------------------------------------------------
+template <int D>
+__device__ __forceinline__ void warp_fwht(float (&v)[D / 32], int lane) {
+  constexpr int E = D / 32;
+#pragma unroll
+  for (int span = 1; span < 32; span <<= 1) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      float other = __shfl_xor_sync(FULL, v[j], span);
+      v[j] = (lane & span) ? __fsub_rn(other, v[j]) : __fadd_rn(v[j], other);
+    }
+  }
+#pragma unroll
+  for (int s = 1; s < E; s <<= 1) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      if ((j & s) == 0) {
+        float a = v[j], b = v[j + s];
+        v[j] = __fadd_rn(a, b);
+        v[j + s] = __fsub_rn(a, b);
+      }
+    }
+  }
+}
+
+// y = second * H(first * x) / f32(sqrt(d)), IEEE division (no reciprocal).
+template <int D>
+__device__ __forceinline__ void warp_rotate(float (&v)[D / 32], int lane, const float* first,
+                                            const float* second) {
+  constexpr int E = D / 32;
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = __fmul_rn(v[j], __ldg(first + j * 32 + lane));
+  warp_fwht<D>(v, lane);
+#pragma unroll
+  for (int j = 0; j < E; ++j)
+    v[j] = __fmul_rn(__fdiv_rn(v[j], SqrtD<D>::v), __ldg(second + j * 32 + lane));
+}
+
+// argmin_k |x - c[k]| over fp32 rounded distances, first index on ties.
+template <int BITS>
+__device__ __forceinline__ uint32_t nearest_code(float x, const float (&c)[1 << BITS]) {
+  uint32_t best = 0;
+  float bd = fabsf(__fsub_rn(x, c[0]));
+#pragma unroll
+  for (int k = 1; k < (1 << BITS); ++k) {
+    float dk = fabsf(__fsub_rn(x, c[k]));
+    if (dk < bd) { bd = dk; best = (uint32_t)k; }
+  }
+  return best;
+}
+
+// Extract code `i` of a packed vector (LSB-first, may straddle two words).
+template <int BITS>
+__device__ __forceinline__ uint32_t code_at(const uint32_t* w, int i) {
+  const int bit = i * BITS;
+  const int wi = bit >> 5, sh = bit & 31;
+  uint32_t v = w[wi] >> sh;
+  if (sh + BITS > 32) v |= w[wi + 1] << (32 - sh);
+  return v & ((1u << BITS) - 1u);
+}
+
+}  // namespace tq

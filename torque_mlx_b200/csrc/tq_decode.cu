@@ -1,0 +1,404 @@
+// Packed-code decode attention (q_len = 1, grouped queries) and the
+// log-sum-exp merges.
+//
+// Split-K ("flash-decoding") structure: the grid is (splits, units); a CTA
+// streams one contiguous token chunk of one (seq, layer, kv_head) unit and
+// serves all G query heads of that kv head from the same code bytes.  Each
+// warp leaves an online-softmax partial (o, m, l) in the workspace; a merge
+// kernel combines the partials of a query row, normalises, optionally
+// rotates the row back by Pi^T and emits the log-sum-exp.
+//
+// Two compute variants share that skeleton:
+//   * exact  — fp32 CUDA-core math with fp32 centroids and query;
+//   * tensor — mma.sync m16n8k16 with fp16 operands (see tq_decode_mma.cuh).
+#include "tq_common.cuh"
+#include "tq_decode_mma.cuh"  // DecodeParams, kMma*
+
+#include <math.h>
+
+namespace tq {
+
+constexpr int kExactWarps = 4;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ---------------------------------------------------------------------------
+// exact fp32 kernel
+//   score phase: lane = token of a 32-token tile, loop over dims;
+//   value phase: lane = dims {lane + 32 i}, loop over the tile's tokens.
+// ---------------------------------------------------------------------------
+template <int D, int BITS, int GM>
+__global__ void __launch_bounds__(kExactWarps * 32)
+decode_exact_kernel(DecodeParams p) {
+  constexpr int W = D * BITS / 32;
+  constexpr int E = D / 32;
+  constexpr int L = 1 << BITS;
+  __shared__ float q_s[GM][D];
+  __shared__ uint32_t tile_s[kExactWarps][32][W + 1];
+  __shared__ float p_s[kExactWarps][32][GM];
+  __shared__ float ck_s[L], cv_s[L];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t u = blockIdx.y;
+  const int split = blockIdx.x;
+  const int G = p.G;
+
+  if (threadIdx.x < L) {
+    ck_s[threadIdx.x] = p.cent_k[threadIdx.x];
+    cv_s[threadIdx.x] = p.cent_v[threadIdx.x];
+  }
+  for (int g = warp; g < GM; g += kExactWarps) {
+    float v[E];
+    if (g < G) {
+      const float* q = p.query + (u * G + g) * D;
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = q[j * 32 + lane];
+      if (p.rotate_query) warp_rotate<D>(v, lane, p.signs_right, p.signs_left);
+    } else {
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < E; ++j) q_s[g][j * 32 + lane] = v[j];
+  }
+  __syncthreads();
+
+  const int64_t n = unit_length(p, u);
+  const int64_t c0 = (int64_t)split * p.chunk;
+  const int64_t c1 = min(c0 + (int64_t)p.chunk, n);
+  const uint32_t* kbase = p.k_slab + u * p.unit_stride;
+  const uint32_t* vbase = p.v_slab + u * p.unit_stride;
+
+  float m[GM], l[GM], acc[GM][E];
+#pragma unroll
+  for (int g = 0; g < GM; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) acc[g][i] = 0.f;
+  }
+
+  for (int64_t t0 = c0 + warp * 32; t0 < c1; t0 += kExactWarps * 32) {
+    const int nt = (int)min((int64_t)32, c1 - t0);
+    // ---- stage K words of the tile (coalesced) ----
+    for (int i = lane; i < nt * W; i += 32) tile_s[warp][i / W][i % W] = kbase[(t0 + i / W) * W + i % W];
+    __syncwarp();
+    float s[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) s[g] = 0.f;
+    if (lane < nt) {
+      uint32_t r[W + 1];
+#pragma unroll
+      for (int w = 0; w < W; ++w) r[w] = tile_s[warp][lane][w];
+      r[W] = 0;
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        const float c = ck_s[code_at<BITS>(r, d)];
+#pragma unroll
+        for (int g = 0; g < GM; ++g) s[g] = fmaf(q_s[g][d], c, s[g]);
+      }
+    }
+    // ---- online softmax over the tile ----
+    float alpha[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+      const float sc = lane < nt ? s[g] * p.scale_log2 : -INFINITY;
+      float tm = sc;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, o));
+      const float mn = fmaxf(m[g], tm);
+      alpha[g] = exp2f(m[g] - mn);  // m = -inf on the first tile -> 0
+      const float pr = lane < nt ? exp2f(sc - mn) : 0.f;
+      float ps = pr;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(FULL, ps, o);
+      l[g] = l[g] * alpha[g] + ps;
+      m[g] = mn;
+      p_s[warp][lane][g] = pr;
+    }
+    __syncwarp();
+    // ---- stage V words, accumulate P.V ----
+    for (int i = lane; i < nt * W; i += 32) tile_s[warp][i / W][i % W] = vbase[(t0 + i / W) * W + i % W];
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < GM; ++g)
+#pragma unroll
+      for (int i = 0; i < E; ++i) acc[g][i] *= alpha[g];
+    for (int t = 0; t < nt; ++t) {
+      const uint32_t* row = tile_s[warp][t];
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        const int dim = lane + 32 * i;
+        const int bit = dim * BITS, wi = bit >> 5, sh = bit & 31;
+        uint32_t cv = row[wi] >> sh;
+        if (sh + BITS > 32) cv |= row[wi + 1] << (32 - sh);
+        const float c = cv_s[cv & (L - 1)];
+#pragma unroll
+        for (int g = 0; g < GM; ++g) acc[g][i] = fmaf(p_s[warp][t][g], c, acc[g][i]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- this warp's partial ----
+  const int nparts = p.splits * kExactWarps;
+  const int part = split * kExactWarps + warp;
+  for (int g = 0; g < G && g < GM; ++g) {
+    float* dst = p.part + ((u * G + g) * nparts + part) * (int64_t)(D + 2);
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[lane + 32 * i] = acc[g][i];
+    if (lane == 0) {
+      dst[D] = m[g];
+      dst[D + 1] = l[g];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// merge the per-warp partials of each query row; optional inverse rotation.
+// One warp per row.
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256)
+merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
+                      float* __restrict__ out, float* __restrict__ lse, int inverse_rotate,
+                      const float* __restrict__ signs_left, const float* __restrict__ signs_right) {
+  constexpr int E = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* base = part + row * nparts * (int64_t)(D + 2);
+  float M = -INFINITY;
+  for (int i = lane; i < nparts; i += 32) {
+    const float li = base[i * (int64_t)(D + 2) + D + 1];
+    if (li > 0.f) M = fmaxf(M, base[i * (int64_t)(D + 2) + D]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+  float v[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = 0.f;
+  float Lsum = 0.f;
+  if (M != -INFINITY) {
+    for (int i = 0; i < nparts; ++i) {
+      const float* pp = base + i * (int64_t)(D + 2);
+      const float li = pp[D + 1];
+      if (!(li > 0.f)) continue;
+      const float w = exp2f(pp[D] - M);
+      Lsum += li * w;
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = fmaf(pp[j * 32 + lane], w, v[j]);
+    }
+    const float inv = 1.f / Lsum;
+#pragma unroll
+    for (int j = 0; j < E; ++j) v[j] *= inv;
+  }
+  if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
+#pragma unroll
+  for (int j = 0; j < E; ++j) out[row * D + j * 32 + lane] = v[j];
+  if (lse && lane == 0) lse[row] = (M == -INFINITY) ? -INFINITY : (M + log2f(Lsum)) * kLn2;
+}
+
+// ---------------------------------------------------------------------------
+// merge normalised parts with natural-log lse (multi-GPU sequence shards)
+// ---------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256)
+lse_merge_kernel(const float* __restrict__ outs, const float* __restrict__ lses, int parts,
+                 int64_t rows, float* __restrict__ out, float* __restrict__ lse_out,
+                 int inverse_rotate, const float* __restrict__ signs_left,
+                 const float* __restrict__ signs_right) {
+  constexpr int E = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float M = -INFINITY;
+  for (int i = lane; i < parts; i += 32) M = fmaxf(M, lses[i * rows + row]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+  float v[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = 0.f;
+  float tot = 0.f;
+  if (M != -INFINITY) {
+    for (int i = 0; i < parts; ++i) {
+      const float s = lses[i * rows + row];
+      if (s == -INFINITY) continue;
+      const float w = expf(s - M);
+      tot += w;
+      const float* o = outs + (i * rows + row) * (int64_t)D;
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = fmaf(o[j * 32 + lane], w, v[j]);
+    }
+    const float inv = 1.f / tot;
+#pragma unroll
+    for (int j = 0; j < E; ++j) v[j] *= inv;
+  }
+  if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
+#pragma unroll
+  for (int j = 0; j < E; ++j) out[row * D + j * 32 + lane] = v[j];
+  if (lse_out && lane == 0) lse_out[row] = (M == -INFINITY) ? -INFINITY : M + logf(tot);
+}
+
+// ---------------------------------------------------------------------------
+// host-side planning
+// ---------------------------------------------------------------------------
+struct Plan {
+  int mode;       // resolved: exact or tensor
+  int chunk;      // tokens per CTA
+  int splits;     // CTAs per unit
+  int warps;      // partials per CTA
+  size_t bytes;   // workspace
+};
+
+static int resolve_mode(int mode, int G) {
+  if (mode == TQ_DECODE_AUTO) return G >= 2 ? TQ_DECODE_TENSOR : TQ_DECODE_EXACT;
+  return mode;
+}
+
+static Plan make_plan(int64_t units, int G, int D, int64_t max_len, int mode) {
+  Plan pl;
+  pl.mode = resolve_mode(mode, G);
+  pl.warps = pl.mode == TQ_DECODE_TENSOR ? 1 : kExactWarps;  // partials per CTA
+  const int tile = pl.mode == TQ_DECODE_TENSOR ? kMmaTokensPerCta : kExactWarps * 32;
+  const int64_t len = max_len < 1 ? 1 : max_len;
+  // aim for >= 4 CTAs per SM on 148 SMs, never below one tile per CTA
+  const int64_t target_ctas = 148 * 4;
+  int64_t splits = (target_ctas + units - 1) / (units < 1 ? 1 : units);
+  const int64_t max_splits = (len + tile - 1) / tile;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  int64_t chunk = (len + splits - 1) / splits;
+  chunk = (chunk + tile - 1) / tile * tile;
+  pl.chunk = (int)chunk;
+  pl.splits = (int)((len + chunk - 1) / chunk);
+  pl.bytes = (size_t)units * G * pl.splits * pl.warps * (size_t)(D + 2) * sizeof(float);
+  return pl;
+}
+
+template <int D, int BITS>
+static void launch_exact(const DecodeParams& p, cudaStream_t st) {
+  dim3 grid(p.splits, (unsigned)p.units);
+  if (p.G <= 1) decode_exact_kernel<D, BITS, 1><<<grid, kExactWarps * 32, 0, st>>>(p);
+  else if (p.G <= 2) decode_exact_kernel<D, BITS, 2><<<grid, kExactWarps * 32, 0, st>>>(p);
+  else if (p.G <= 4) decode_exact_kernel<D, BITS, 4><<<grid, kExactWarps * 32, 0, st>>>(p);
+  else if (p.G <= 8) decode_exact_kernel<D, BITS, 8><<<grid, kExactWarps * 32, 0, st>>>(p);
+  else decode_exact_kernel<D, BITS, 16><<<grid, kExactWarps * 32, 0, st>>>(p);
+}
+
+template <int D>
+static void launch_decode_d(int bits, int mode, const DecodeParams& p, cudaStream_t st) {
+  if (mode == TQ_DECODE_TENSOR) {
+    launch_mma_dispatch(D, bits, p, st);
+  } else {
+    if (bits == 2) launch_exact<D, 2>(p, st);
+    else if (bits == 3) launch_exact<D, 3>(p, st);
+    else launch_exact<D, 4>(p, st);
+  }
+}
+
+template <int D>
+static void launch_merge(const float* part, int nparts, int64_t rows, float* out, float* lse,
+                         int inv, const float* sl, const float* sr, cudaStream_t st) {
+  merge_partials_kernel<D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(part, nparts, rows, out, lse,
+                                                                         inv, sl, sr);
+}
+
+}  // namespace tq
+
+using namespace tq;
+
+extern "C" {
+
+int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int64_t max_len,
+                             int mode, size_t* bytes) {
+  if (!bytes) return TQ_E_ARG;
+  if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
+  if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
+  if (mode < TQ_DECODE_AUTO || mode > TQ_DECODE_TENSOR) return TQ_E_ARG;
+  *bytes = make_plan(units, group_size, head_dim, max_len, mode).bytes;
+  return TQ_OK;
+}
+
+int tq_decode(const float* query, int rotate_query, const float* signs_left,
+              const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
+              int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
+              int64_t len_offset, int64_t max_len, int64_t units, int group_size, int head_dim,
+              int bits, const float* cent_k, const float* cent_v, float scale, float* out,
+              float* lse, int inverse_rotate_output, int mode, void* workspace,
+              size_t workspace_bytes, tq_stream_t stream) {
+  if (!valid_bits(bits)) return TQ_E_BITS;
+  if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
+  if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
+  if (mode < TQ_DECODE_AUTO || mode > TQ_DECODE_TENSOR) return TQ_E_ARG;
+  if (units == 0) return TQ_OK;
+  if (!query || !k_slab || !v_slab || !cent_k || !cent_v || !out) return TQ_E_ARG;
+  if ((rotate_query || inverse_rotate_output) && (!signs_left || !signs_right)) return TQ_E_ARG;
+  if (lengths && units_per_seq <= 0) return TQ_E_ARG;
+  const int W = words_for(head_dim, bits);
+  if (unit_stride_words < max_len * W) return TQ_E_SHAPE;
+  // the bulk-copy engine needs 16-byte aligned rows of whole 16-byte blocks
+  const bool aligned = ((uintptr_t)k_slab % 16 == 0) && ((uintptr_t)v_slab % 16 == 0) &&
+                       (unit_stride_words % 4 == 0);
+  if (!aligned) {
+    if (mode == TQ_DECODE_TENSOR) return TQ_E_SHAPE;
+    mode = TQ_DECODE_EXACT;
+  }
+  const Plan pl = make_plan(units, group_size, head_dim, max_len, mode);
+  if (!workspace || workspace_bytes < pl.bytes) return TQ_E_WORKSPACE;
+  if (units > 65535) return TQ_E_SHAPE;  // grid.y limit
+
+  DecodeParams p;
+  p.query = query;
+  p.rotate_query = rotate_query;
+  p.signs_left = signs_left;
+  p.signs_right = signs_right;
+  p.k_slab = k_slab;
+  p.v_slab = v_slab;
+  p.unit_stride = unit_stride_words;
+  p.lengths = lengths;
+  p.units_per_seq = units_per_seq;
+  p.len_offset = len_offset;
+  p.max_len = max_len;
+  p.units = units;
+  p.G = group_size;
+  p.cent_k = cent_k;
+  p.cent_v = cent_v;
+  p.scale_log2 = scale * kLog2e;
+  p.chunk = pl.chunk;
+  p.splits = pl.splits;
+  p.part = (float*)workspace;
+  p.err = nullptr;
+
+  cudaStream_t st = (cudaStream_t)stream;
+  if (head_dim == 64) launch_decode_d<64>(bits, pl.mode, p, st);
+  else if (head_dim == 128) launch_decode_d<128>(bits, pl.mode, p, st);
+  else launch_decode_d<256>(bits, pl.mode, p, st);
+  int s = launch_status();
+  if (s != TQ_OK) return s;
+
+  const int nparts = pl.splits * pl.warps;
+  const int64_t rows = units * group_size;
+  if (head_dim == 64) launch_merge<64>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, st);
+  else if (head_dim == 128) launch_merge<128>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, st);
+  else launch_merge<256>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, st);
+  return launch_status();
+}
+
+int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, int head_dim,
+                 float* out, float* lse_out, int inverse_rotate, const float* signs_left,
+                 const float* signs_right, tq_stream_t stream) {
+  if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
+  if (parts < 1 || rows < 0) return TQ_E_SHAPE;
+  if (rows == 0) return TQ_OK;
+  if (!outs || !lses || !out) return TQ_E_ARG;
+  if (inverse_rotate && (!signs_left || !signs_right)) return TQ_E_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (head_dim == 64) lse_merge_kernel<64><<<grid, 256, 0, st>>>(outs, lses, parts, rows, out, lse_out, inverse_rotate, signs_left, signs_right);
+  else if (head_dim == 128) lse_merge_kernel<128><<<grid, 256, 0, st>>>(outs, lses, parts, rows, out, lse_out, inverse_rotate, signs_left, signs_right);
+  else lse_merge_kernel<256><<<grid, 256, 0, st>>>(outs, lses, parts, rows, out, lse_out, inverse_rotate, signs_left, signs_right);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,254 @@
+"""Packed-code operators on explicit device tensors.
+
+These mirror the reference's kernel wrappers in src/torque_mlx/mlx_ops.py
+(same names, argument meaning and errors) but run the sm_100a kernels of
+``libtorque_b200.so`` instead of Metal.  Code tensors hold uint32 words in the
+reference's LSB-first layout; torch tensors may be ``torch.uint32`` or
+``torch.int32`` storage.  Queries given to the ``decode_packed_*`` functions
+are already rotated, as in the reference.
+"""
+
+from __future__ import annotations
+
+from math import sqrt
+
+import numpy as np
+import torch
+
+from . import _lib, _tensors
+from .quantization import Codebook, packed_words_for_head_dim
+
+_MODES = {"auto": _lib.DECODE_AUTO, "exact": _lib.DECODE_EXACT, "tensor": _lib.DECODE_TENSOR}
+
+
+def cuda_available() -> bool:
+    """Counterpart of ``metal_available`` (mlx_ops.py:34-45)."""
+    try:
+        _lib.load()
+        return True
+    except RuntimeError:
+        return False
+
+
+def decode_mode_code(mode: str | int) -> int:
+    if isinstance(mode, int):
+        return mode
+    try:
+        return _MODES[mode]
+    except KeyError as exc:
+        raise ValueError(f"decode mode must be one of {sorted(_MODES)}") from exc
+
+
+class Workspace:
+    """Grow-only device scratch buffer for the split-K partials."""
+
+    def __init__(self) -> None:
+        self.buf: torch.Tensor | None = None
+
+    def get(self, nbytes: int, device: torch.device) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
+            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+        return self.buf
+
+
+_default_ws = Workspace()
+
+
+def workspace_bytes(units: int, group_size: int, head_dim: int, max_len: int, mode: str | int = "auto") -> int:
+    lib = _lib.load(require_cuda=False)
+    out = _lib.c_size_t(0)
+    _lib.check(lib.tq_decode_workspace_size(units, group_size, head_dim, max_len, decode_mode_code(mode),
+                                            _lib.ctypes.byref(out)), "decode workspace")
+    return int(out.value)
+
+
+def decode_raw(*, query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tensor, unit_stride: int,
+               lengths: torch.Tensor | None, units_per_seq: int, len_offset: int, max_len: int, units: int,
+               group_size: int, head_dim: int, bits: int, cent_k: torch.Tensor, cent_v: torch.Tensor,
+               out: torch.Tensor, lse: torch.Tensor | None = None, rotate_query: bool = False,
+               inverse_rotate: bool = False, signs: tuple[torch.Tensor, torch.Tensor] | None = None,
+               scale: float | None = None, mode: str | int = "auto", workspace: Workspace | None = None) -> None:
+    """One ``tq_decode`` call on prepared device tensors (see include/torque_b200.h)."""
+    lib = _lib.load()
+    ws = (workspace or _default_ws).get(workspace_bytes(units, group_size, head_dim, max_len, mode), out.device)
+    sl, sr = signs if signs is not None else (None, None)
+    _lib.check(lib.tq_decode(
+        query.data_ptr(), int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(), v_slab.data_ptr(),
+        unit_stride, _lib.ptr(lengths), units_per_seq, len_offset, max_len, units, group_size, head_dim, bits,
+        cent_k.data_ptr(), cent_v.data_ptr(), float(1.0 / sqrt(head_dim) if scale is None else scale),
+        out.data_ptr(), _lib.ptr(lse), int(inverse_rotate), decode_mode_code(mode), ws.data_ptr(), ws.numel(),
+        _lib.stream_ptr()), "decode")
+
+
+def _cent(c) -> torch.Tensor:
+    if isinstance(c, Codebook):
+        c = c.centroids
+    return _tensors.to_cuda(c, torch.float32)
+
+
+def _check_codes(codes: torch.Tensor, bit_width: int, head_dim: int, name: str) -> int:
+    W = packed_words_for_head_dim(head_dim, bit_width)
+    if codes.shape[-1] != W:
+        raise ValueError(f"packed width mismatch for {name}: expected {W}, got {codes.shape[-1]}")
+    return W
+
+
+def decode_packed_attention_split_batched(query, k_codes, v_codes, centroids_k, centroids_v, *,
+                                          bit_width: int, head_dim: int, mode: str = "auto",
+                                          return_lse: bool = False):
+    """softmax(q.K^T / sqrt(d)) V per batch row over packed codes
+    (mlx_ops.py:571-595).  query [BH, d]; k/v codes [BH, L, W] -> [BH, d]."""
+    np_out = _tensors.is_numpy(query)
+    q = _tensors.to_cuda(query, torch.float32)
+    kc = _tensors.words_to_cuda(k_codes)
+    vc = _tensors.words_to_cuda(v_codes)
+    if q.dim() != 2 or q.shape[1] != head_dim:
+        raise ValueError(f"batched query must have shape (batch, {head_dim}), got {tuple(q.shape)}")
+    W = _check_codes(kc, bit_width, head_dim, "k_codes")
+    _check_codes(vc, bit_width, head_dim, "v_codes")
+    if kc.dim() != 3 or kc.shape != vc.shape or kc.shape[0] != q.shape[0]:
+        raise ValueError("batched packed codes must have shape (batch, seq, packed_words) matching the query")
+    B, L = int(kc.shape[0]), int(kc.shape[1])
+    out = torch.empty((B, head_dim), dtype=torch.float32, device=q.device)
+    lse = torch.empty((B,), dtype=torch.float32, device=q.device)
+    decode_raw(query=q, k_slab=kc, v_slab=vc, unit_stride=L * W, lengths=None, units_per_seq=1, len_offset=L,
+               max_len=L, units=B, group_size=1, head_dim=head_dim, bits=bit_width, cent_k=_cent(centroids_k),
+               cent_v=_cent(centroids_v), out=out, lse=lse, mode=mode)
+    if return_lse:
+        return _tensors.out(out, np_out), _tensors.out(lse, np_out)
+    return _tensors.out(out, np_out)
+
+
+def decode_packed_attention(query, k_codes, v_codes, centroids_k, centroids_v, *, bit_width: int,
+                            head_dim: int, mode: str = "auto"):
+    """Single-head fused decode (mlx_ops.py:663-692): query [d]; codes [L, W] -> [d]."""
+    np_out = _tensors.is_numpy(query)
+    q = _tensors.to_cuda(query, torch.float32).reshape(1, -1)
+    kc = _tensors.words_to_cuda(k_codes)
+    vc = _tensors.words_to_cuda(v_codes)
+    W = packed_words_for_head_dim(head_dim, bit_width)
+    if kc.shape[-1] != W or vc.shape[-1] != W:
+        raise ValueError("packed width mismatch for fused decode kernel")
+    res = decode_packed_attention_split_batched(q, kc.reshape(1, -1, W), vc.reshape(1, -1, W), centroids_k,
+                                                centroids_v, bit_width=bit_width, head_dim=head_dim, mode=mode)
+    return _tensors.out(res[0], np_out)
+
+
+decode_packed_attention_split = decode_packed_attention
+
+
+def decode_packed_attention_split_batched_with_current(query, k_codes, v_codes, centroids_k, centroids_v,
+                                                       current_keys, current_values, *, bit_width: int,
+                                                       head_dim: int, mode: str = "auto"):
+    """Attend packed codes plus one dense current token per row
+    (mlx_ops.py:598-660).  The packed part is one ``tq_decode`` (which also
+    yields its log-sum-exp); the current token is a second softmax part with
+    lse = its scaled score, and ``tq_lse_merge`` combines the two exactly."""
+    lib = _lib.load()
+    np_out = _tensors.is_numpy(query)
+    q = _tensors.to_cuda(query, torch.float32)
+    ck = _tensors.to_cuda(current_keys, torch.float32)
+    cv = _tensors.to_cuda(current_values, torch.float32)
+    if q.dim() != 2 or q.shape[1] != head_dim:
+        raise ValueError(f"batched query must have shape (batch, {head_dim}), got {tuple(q.shape)}")
+    if ck.shape != q.shape:
+        raise ValueError(f"current_keys must have shape {tuple(q.shape)}, got {tuple(ck.shape)}")
+    if cv.shape != q.shape:
+        raise ValueError(f"current_values must have shape {tuple(q.shape)}, got {tuple(cv.shape)}")
+    kc = _tensors.words_to_cuda(k_codes)
+    vc = _tensors.words_to_cuda(v_codes)
+    if kc.dim() != 3 or vc.dim() != 3:
+        raise ValueError("packed codes must have shape (batch, seq, packed_words)")
+    if kc.shape != vc.shape:
+        raise ValueError(f"k_codes and v_codes must match, got {tuple(kc.shape)} and {tuple(vc.shape)}")
+    if kc.shape[0] != q.shape[0]:
+        raise ValueError("packed codes and query must agree on batch dimension")
+    B = q.shape[0]
+    if kc.shape[1] == 0:
+        return _tensors.out(cv.clone(), np_out)
+    outs = torch.empty((2, B, head_dim), dtype=torch.float32, device=q.device)
+    lses = torch.empty((2, B), dtype=torch.float32, device=q.device)
+    o, s = decode_packed_attention_split_batched(q, kc, vc, centroids_k, centroids_v, bit_width=bit_width,
+                                                 head_dim=head_dim, mode=mode, return_lse=True)
+    outs[0].copy_(o)
+    lses[0].copy_(s)
+    outs[1].copy_(cv)
+    lses[1].copy_((q * ck).sum(dim=1) * (1.0 / sqrt(head_dim)))
+    res = torch.empty((B, head_dim), dtype=torch.float32, device=q.device)
+    _lib.check(lib.tq_lse_merge(outs.data_ptr(), lses.data_ptr(), 2, B, head_dim, res.data_ptr(), None, 0, None,
+                                None, _lib.stream_ptr()), "lse merge")
+    return _tensors.out(res, np_out)
+
+
+def lse_merge(outs: torch.Tensor, lses: torch.Tensor, *, out: torch.Tensor | None = None,
+              lse_out: torch.Tensor | None = None, inverse_rotation=None) -> torch.Tensor:
+    """Merge P normalised partial attentions ``outs [P, rows, d]`` with their
+    natural-log ``lses [P, rows]`` (``tq_lse_merge``); optionally rotate the
+    merged rows back with ``inverse_rotation`` (a RotationSpec)."""
+    lib = _lib.load()
+    P, rows, d = outs.shape
+    res = out if out is not None else torch.empty((rows, d), dtype=torch.float32, device=outs.device)
+    sl = sr = None
+    if inverse_rotation is not None:
+        sl, sr = inverse_rotation.device_signs()
+    _lib.check(lib.tq_lse_merge(outs.contiguous().data_ptr(), lses.contiguous().data_ptr(), P, rows, d,
+                                res.data_ptr(), _lib.ptr(lse_out), int(inverse_rotation is not None),
+                                _lib.ptr(sl), _lib.ptr(sr), _lib.stream_ptr()), "lse merge")
+    return res
+
+
+def quantize_and_pack_rows(values, codebook, *, bit_width: int, head_dim: int, rotation=None):
+    """Quantize + pack rows ``[R, d]`` into words ``[R, W]`` in one launch
+    (mlx_ops.py:342-371).  Unlike the Metal kernel, which counts boundaries,
+    this uses the reference numpy quantizer's nearest-centroid rule
+    (quantization.py:120-125), so it needs the codebook itself.  ``rotation``
+    (a RotationSpec) rotates the rows first, fused in the same kernel."""
+    return quantize_and_pack_rows_dual(values, None, codebook, None, bit_width=bit_width, head_dim=head_dim,
+                                       rotation=rotation)[0]
+
+
+def quantize_and_pack_rows_dual(values_a, values_b, codebook_a, codebook_b, *, bit_width: int, head_dim: int,
+                                rotation=None):
+    """K and V rows in one launch (mlx_ops.py:374-412)."""
+    lib = _lib.load()
+    np_out = _tensors.is_numpy(values_a)
+    a = _tensors.to_cuda(values_a, torch.float32, keep_half=True)
+    if a.dim() != 2 or a.shape[1] != head_dim:
+        raise ValueError(f"values_a must have shape (rows, {head_dim}), got {tuple(a.shape)}")
+    b = None
+    if values_b is not None:
+        b = _tensors.to_cuda(values_b, torch.float32, keep_half=True).to(a.dtype)
+        if b.shape != a.shape:
+            raise ValueError(f"values_a and values_b must match, got {tuple(a.shape)} and {tuple(b.shape)}")
+    W = packed_words_for_head_dim(head_dim, bit_width)
+    R = int(a.shape[0])
+    wa = torch.empty((R, W), dtype=torch.int32, device=a.device)
+    wb = torch.empty((R, W), dtype=torch.int32, device=a.device) if b is not None else None
+    ca = _cent(codebook_a)
+    cb = _cent(codebook_b) if b is not None else None
+    sl = sr = None
+    if rotation is not None:
+        sl, sr = rotation.device_signs()
+    _lib.check(lib.tq_append_kv(a.data_ptr(), _lib.ptr(b), _lib.dtype_code(a.dtype), R, 1, head_dim, bit_width,
+                                _lib.ptr(sl), _lib.ptr(sr), int(rotation is not None), ca.data_ptr(), _lib.ptr(cb),
+                                wa.data_ptr(), _lib.ptr(wb), W, 1, None, 1, 0, _lib.stream_ptr()), "append")
+    ra = _tensors.words_out(wa, np_out)
+    rb = _tensors.words_out(wb, np_out) if wb is not None else None
+    return ra, rb
+
+
+def dequantize_packed(words, codebook, *, bit_width: int, head_dim: int):
+    """centroids[unpack(words)] for rows of packed words -> fp32 ``[..., d]``."""
+    lib = _lib.load()
+    np_out = _tensors.is_numpy(words)
+    w = _tensors.words_to_cuda(words)
+    _check_codes(w, bit_width, head_dim, "words")
+    rows = w.numel() // w.shape[-1]
+    out = torch.empty((*w.shape[:-1], head_dim), dtype=torch.float32, device=w.device)
+    _lib.check(lib.tq_dequantize_packed(w.data_ptr(), out.data_ptr(), rows, head_dim, bit_width,
+                                        _cent(codebook).data_ptr(), _lib.stream_ptr()), "dequantize")
+    return _tensors.out(out, np_out)
+
+
+def as_numpy_words(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int32).cpu().numpy().view(np.uint32)
