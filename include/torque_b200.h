@@ -119,8 +119,9 @@ int tq_lengths_add(int32_t* lengths, int n, int delta, tq_stream_t stream);
  * Decode attention over packed codes
  * ------------------------------------------------------------------------- */
 
-/* Bytes of workspace tq_decode needs for these sizes. */
-int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int64_t max_len,
+/* Bytes of workspace tq_decode needs for these sizes (on the current device:
+ * the split plan follows its SM count and the kernel's occupancy). */
+int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int bits, int64_t max_len,
                              int mode, size_t* bytes);
 
 /* Grouped-query decode attention (q_len = 1) straight on packed codes.

@@ -60,8 +60,8 @@ def test_host_side_argument_checks(built_lib):
     assert lib.tq_quantize(None, None, 4, None, 5, None) == _lib.TQ_E_BITS
     assert lib.tq_pack(None, None, 0, 0, 3, None) == _lib.TQ_OK  # empty is a no-op
     size = ctypes.c_size_t()
-    assert lib.tq_decode_workspace_size(4, 17, 128, 100, 0, ctypes.byref(size)) == _lib.TQ_E_SHAPE
-    assert lib.tq_decode_workspace_size(4, 4, 128, 100, 0, ctypes.byref(size)) == _lib.TQ_OK
+    assert lib.tq_decode_workspace_size(4, 17, 128, 4, 100, 0, ctypes.byref(size)) == _lib.TQ_E_SHAPE
+    assert lib.tq_decode_workspace_size(4, 4, 128, 4, 100, 0, ctypes.byref(size)) == _lib.TQ_OK
     assert size.value > 0
     assert lib.tq_decode(None, 0, None, None, None, None, 0, None, 1, 0, 0, 1, 1, 128, 4, None, None, 1.0,
                          None, None, 0, 0, None, 0, None) == _lib.TQ_E_ARG

@@ -45,7 +45,7 @@ SIGNATURES: dict[str, tuple] = {
                              c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                              c_int, c_int64, c_void_p]),
     "tq_lengths_add": (c_int, [c_void_p, c_int, c_int, c_void_p]),
-    "tq_decode_workspace_size": (c_int, [c_int64, c_int, c_int, c_int64, c_int, POINTER(c_size_t)]),
+    "tq_decode_workspace_size": (c_int, [c_int64, c_int, c_int, c_int, c_int64, c_int, POINTER(c_size_t)]),
     "tq_decode": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
                           c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
                           c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),

@@ -155,43 +155,69 @@ decode_exact_kernel(DecodeParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// merge the per-warp partials of each query row; optional inverse rotation.
-// One warp per row.
+// merge the split partials (o unnormalised, m in log2 units, l) of each query
+// row; optional inverse rotation.  One CTA per row: its warps take the parts
+// round-robin, so rows with many splits (long single sequences) merge in
+// parallel instead of one warp walking every part.
 // ---------------------------------------------------------------------------
+constexpr int kMergeWarps = 8;
+
 template <int D>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kMergeWarps * 32)
 merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
                       float* __restrict__ out, float* __restrict__ lse, int inverse_rotate,
                       const float* __restrict__ signs_left, const float* __restrict__ signs_right) {
   constexpr int E = D / 32;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  __shared__ float red[kMergeWarps][D];
+  __shared__ float red_l[kMergeWarps];
+  __shared__ float sM;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
   const float* base = part + row * nparts * (int64_t)(D + 2);
-  float M = -INFINITY;
-  for (int i = lane; i < nparts; i += 32) {
-    const float li = base[i * (int64_t)(D + 2) + D + 1];
-    if (li > 0.f) M = fmaxf(M, base[i * (int64_t)(D + 2) + D]);
+  float M = -INFINITY;  // max over parts that saw tokens
+  for (int i = threadIdx.x; i < nparts; i += kMergeWarps * 32) {
+    const float* pp = base + i * (int64_t)(D + 2);
+    if (pp[D + 1] > 0.f) M = fmaxf(M, pp[D]);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+  if (lane == 0) red_l[warp] = M;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < kMergeWarps; ++w) m = fmaxf(m, red_l[w]);
+    sM = m;
+  }
+  __syncthreads();
+  M = sM;
   float v[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) v[j] = 0.f;
-  float Lsum = 0.f;
+  float Lw = 0.f;
   if (M != -INFINITY) {
-    for (int i = 0; i < nparts; ++i) {
+    for (int i = warp; i < nparts; i += kMergeWarps) {
       const float* pp = base + i * (int64_t)(D + 2);
       const float li = pp[D + 1];
       if (!(li > 0.f)) continue;
       const float w = exp2f(pp[D] - M);
-      Lsum += li * w;
+      Lw += li * w;
 #pragma unroll
       for (int j = 0; j < E; ++j) v[j] = fmaf(pp[j * 32 + lane], w, v[j]);
     }
-    const float inv = 1.f / Lsum;
+  }
+  __syncthreads();
 #pragma unroll
-    for (int j = 0; j < E; ++j) v[j] *= inv;
+  for (int j = 0; j < E; ++j) red[warp][j * 32 + lane] = v[j];
+  if (lane == 0) red_l[warp] = Lw;
+  __syncthreads();
+  if (warp != 0) return;
+  float Lsum = 0.f;
+  for (int w = 0; w < kMergeWarps; ++w) Lsum += red_l[w];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    float acc = 0.f;
+    for (int w = 0; w < kMergeWarps; ++w) acc += red[w][j * 32 + lane];
+    v[j] = M == -INFINITY ? 0.f : acc / Lsum;
   }
   if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
 #pragma unroll
@@ -256,15 +282,30 @@ static int resolve_mode(int mode, int G) {
   return mode;
 }
 
-static Plan make_plan(int64_t units, int G, int D, int64_t max_len, int mode) {
+static int sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) {
+    cudaGetLastError();
+    sms = 148;  // B200
+  }
+  return sms;
+}
+
+// Split planning.  Few units (long single sequences): one full wave of
+// resident CTAs, so every SM streams and each CTA's fixed cost (tables,
+// query rotation, merge) is paid once.  Many units (batched decode): about
+// four waves, so ragged lengths balance across SMs.
+static Plan make_plan(int64_t units, int G, int D, int bits, int64_t max_len, int mode) {
   Plan pl;
   pl.mode = resolve_mode(mode, G);
   pl.warps = pl.mode == TQ_DECODE_TENSOR ? 1 : kExactWarps;  // partials per CTA
   const int tile = pl.mode == TQ_DECODE_TENSOR ? kMmaTokensPerCta : kExactWarps * 32;
+  const int per_sm = pl.mode == TQ_DECODE_TENSOR ? mma_blocks_per_sm(D, bits, G) : 4;
+  const int64_t wave = (int64_t)sm_count() * per_sm;
   const int64_t len = max_len < 1 ? 1 : max_len;
-  // aim for >= 4 CTAs per SM on 148 SMs, never below one tile per CTA
-  const int64_t target_ctas = 148 * 4;
-  int64_t splits = (target_ctas + units - 1) / (units < 1 ? 1 : units);
+  const int64_t uu = units < 1 ? 1 : units;
+  int64_t splits = uu < wave ? (wave + uu - 1) / uu : (4 * wave + uu - 1) / uu;
   const int64_t max_splits = (len + tile - 1) / tile;
   if (splits > max_splits) splits = max_splits;
   if (splits < 1) splits = 1;
@@ -300,8 +341,8 @@ static void launch_decode_d(int bits, int mode, const DecodeParams& p, cudaStrea
 template <int D>
 static void launch_merge(const float* part, int nparts, int64_t rows, float* out, float* lse,
                          int inv, const float* sl, const float* sr, cudaStream_t st) {
-  merge_partials_kernel<D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(part, nparts, rows, out, lse,
-                                                                         inv, sl, sr);
+  merge_partials_kernel<D><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(part, nparts, rows, out, lse, inv,
+                                                                        sl, sr);
 }
 
 }  // namespace tq
@@ -310,13 +351,14 @@ using namespace tq;
 
 extern "C" {
 
-int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int64_t max_len,
+int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int bits, int64_t max_len,
                              int mode, size_t* bytes) {
   if (!bytes) return TQ_E_ARG;
+  if (!valid_bits(bits)) return TQ_E_BITS;
   if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
   if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
   if (mode < TQ_DECODE_AUTO || mode > TQ_DECODE_TENSOR) return TQ_E_ARG;
-  *bytes = make_plan(units, group_size, head_dim, max_len, mode).bytes;
+  *bytes = make_plan(units, group_size, head_dim, bits, max_len, mode).bytes;
   return TQ_OK;
 }
 
@@ -344,7 +386,7 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
     if (mode == TQ_DECODE_TENSOR) return TQ_E_SHAPE;
     mode = TQ_DECODE_EXACT;
   }
-  const Plan pl = make_plan(units, group_size, head_dim, max_len, mode);
+  const Plan pl = make_plan(units, group_size, head_dim, bits, max_len, mode);
   if (!workspace || workspace_bytes < pl.bytes) return TQ_E_WORKSPACE;
   if (units > 65535) return TQ_E_SHAPE;  // grid.y limit
 
@@ -368,7 +410,6 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
   p.chunk = pl.chunk;
   p.splits = pl.splits;
   p.part = (float*)workspace;
-  p.err = nullptr;
 
   cudaStream_t st = (cudaStream_t)stream;
   if (head_dim == 64) launch_decode_d<64>(bits, pl.mode, p, st);

@@ -3,35 +3,70 @@
 
 namespace tq {
 
+template <int D, int BITS, int NT>
+static void* prepare() {
+  // the dynamic shared-memory opt-in, once per process (it is per-function state)
+  static const bool done = [] {
+    cudaFuncSetAttribute(decode_mma_kernel<D, BITS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)MmaCfg<D, BITS, NT>::SMEM_BYTES);
+    return true;
+  }();
+  (void)done;
+  return (void*)decode_mma_kernel<D, BITS, NT>;
+}
+
+template <int D, int BITS, int NT>
+static int occupancy() {
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, prepare<D, BITS, NT>(), kMmaWarps * 32,
+                                                    MmaCfg<D, BITS, NT>::SMEM_BYTES) != cudaSuccess ||
+      blocks < 1) {
+    cudaGetLastError();
+    blocks = mma_min_blocks<D>();
+  }
+  return blocks;
+}
+
 template <int D, int BITS>
 static void launch_mma(const DecodeParams& p, cudaStream_t st) {
   dim3 grid(p.splits, (unsigned)p.units);
   if (p.G <= 8) {
-    constexpr size_t smem = MmaCfg<D, BITS, 1>::SMEM_BYTES;
-    cudaFuncSetAttribute(decode_mma_kernel<D, BITS, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    decode_mma_kernel<D, BITS, 1><<<grid, kMmaWarps * 32, smem, st>>>(p);
+    prepare<D, BITS, 1>();
+    decode_mma_kernel<D, BITS, 1><<<grid, kMmaWarps * 32, MmaCfg<D, BITS, 1>::SMEM_BYTES, st>>>(p);
   } else {
-    constexpr size_t smem = MmaCfg<D, BITS, 2>::SMEM_BYTES;
-    cudaFuncSetAttribute(decode_mma_kernel<D, BITS, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    decode_mma_kernel<D, BITS, 2><<<grid, kMmaWarps * 32, smem, st>>>(p);
+    prepare<D, BITS, 2>();
+    decode_mma_kernel<D, BITS, 2><<<grid, kMmaWarps * 32, MmaCfg<D, BITS, 2>::SMEM_BYTES, st>>>(p);
   }
 }
 
+template <int D, int BITS>
+static int blocks_for(int G) {
+  return G <= 8 ? occupancy<D, BITS, 1>() : occupancy<D, BITS, 2>();
+}
+
+#define TQ_DISPATCH(D_, bits_, CALL)                                   \
+  do {                                                                 \
+    if (D_ == 64) {                                                    \
+      if (bits_ == 2) CALL(64, 2); else if (bits_ == 3) CALL(64, 3); else CALL(64, 4); \
+    } else if (D_ == 128) {                                            \
+      if (bits_ == 2) CALL(128, 2); else if (bits_ == 3) CALL(128, 3); else CALL(128, 4); \
+    } else {                                                           \
+      if (bits_ == 2) CALL(256, 2); else if (bits_ == 3) CALL(256, 3); else CALL(256, 4); \
+    }                                                                  \
+  } while (0)
 
 void launch_mma_dispatch(int D, int bits, const DecodeParams& p, cudaStream_t st) {
-  if (D == 64) {
-    if (bits == 2) launch_mma<64, 2>(p, st);
-    else if (bits == 3) launch_mma<64, 3>(p, st);
-    else launch_mma<64, 4>(p, st);
-  } else if (D == 128) {
-    if (bits == 2) launch_mma<128, 2>(p, st);
-    else if (bits == 3) launch_mma<128, 3>(p, st);
-    else launch_mma<128, 4>(p, st);
-  } else {
-    if (bits == 2) launch_mma<256, 2>(p, st);
-    else if (bits == 3) launch_mma<256, 3>(p, st);
-    else launch_mma<256, 4>(p, st);
-  }
+#define CALL_LAUNCH(d, b) launch_mma<d, b>(p, st)
+  TQ_DISPATCH(D, bits, CALL_LAUNCH);
+#undef CALL_LAUNCH
+}
+
+int mma_blocks_per_sm(int D, int bits, int G) {
+  int r = 1;
+#define CALL_OCC(d, b) r = blocks_for<d, b>(G)
+  TQ_DISPATCH(D, bits, CALL_OCC);
+#undef CALL_OCC
+  return r;
 }
 
 }  // namespace tq

@@ -1,29 +1,35 @@
 // Tensor-core packed decode attention (sm_100a, mma.sync m16n8k16 f16 -> f32).
 //
-// Per CTA: one token chunk of one (seq, layer, kv_head) unit, NW warps.
+// Grid (splits, units); a CTA takes one token chunk of one (seq, layer,
+// kv_head) unit and gives each of its NW warps a contiguous sub-range, so the
+// warps run independent software pipelines (no barrier in the token loop).
 //
-//  * K/V code bytes are streamed HBM -> shared memory by the bulk-copy engine
-//    (cp.async.bulk, completion on an mbarrier) through a ring of RS stages of
-//    NW*16 tokens each, so loads stay in flight while warps compute.
-//  * A code pair (two b-bit indices, 2b bits) is turned into a half2 of
-//    centroids by ONE 32-bit shared load from a pair table: entry e holds
-//    (c[e & (2^b-1)], c[e >> b]).  Every lane has its own copy of the table in
-//    its own bank (entry e of lane l at word e*32 + l), so lookups never
+//  * Codes stream HBM -> registers with coalesced vector loads (a warp load
+//    instruction covers whole token rows); the next 16-token tile is loaded
+//    while the current one is computed (two register sets, ping-pong).
+//  * A code pair (two b-bit indices) becomes a half2 of centroids with ONE
+//    32-bit shared-memory load from a pair table: entry e holds
+//    (c[e & (2^b-1)], c[e >> b]).  Every lane owns a private copy of the table
+//    in its own bank (entry e of lane l at word e*32 + l), so lookups never
 //    conflict whatever the codes are.
-//  * scores:  S[t, g] = K[t, :] . Qs[g, :]   as M = 16 tokens, N = 8 query
-//    heads, K = 16 dims per mma.  Lane (r = lane/4, c = lane%4) takes the
-//    contiguous run of d/4 dims [c*d/4, (c+1)*d/4) for its two token rows, so
-//    it reads whole words and no code is read twice; the query fragments use
-//    the same dim permutation (a sum over dims does not depend on its order).
-//  * values:  O^T[dim, g] = V^T[dim, t] . P^T[t, g]  as M = 16 dims,
-//    N = 8 heads, K = 16 tokens.  Lane r owns the run of d/8 dims
-//    [r*d/8, (r+1)*d/8); the two codes of consecutive tokens at one dim are
-//    interleaved in registers (SWAR for 2/4 bits) into the same pair index.
-//  * online softmax in fp32 (base-2, scale folded into the query), the
-//    probabilities are rounded to fp16 once and used for both P.V and the
-//    denominator, so the weights of a row sum to one.
-//  * the NW warps of a CTA are merged in shared memory and one partial
-//    (o, m, l) per query row is written for the split merge kernel.
+//  * scores  S[t, g] = K[t, :] . Qs[g, :]  as M = 16 tokens, N = 8 heads,
+//    K = 16 dims per mma.  Lane (r = lane/4, c = lane%4) takes the contiguous
+//    run of d/4 dims [c*d/4, (c+1)*d/4) of its two token rows, so every code
+//    is loaded once; the query fragments use the same dim permutation (a sum
+//    over dims does not depend on its order).
+//  * values  O^T[dim, g] = V^T[dim, t] . P^T[t, g]  as M = 16 dims, N = 8
+//    heads, K = 16 tokens.  Lane r owns the run of d/8 dims [r*d/8, (r+1)*d/8);
+//    the codes of tokens t and t+1 at one dim are interleaved in registers
+//    (mask + funnel shift) into the same pair index.
+//  * online softmax in base 2 (scale folded into the query) with a lazy
+//    reference max: probabilities are exp2(s - m) with m shared by the lanes of
+//    a head; m is only raised (shuffle max + rescale) when a score exceeds it
+//    by more than 8, so p <= 256 stays exact in fp16 and most tiles need no
+//    cross-lane reduction.  P is rounded to fp16 once and the same values feed
+//    P.V and the denominator.  The C->B fragment transpose of P is movmatrix.
+//  * the warps' accumulators are merged through shared memory (fragment
+//    slabs, read back conflict-free); one partial (o, m, l) per query row and
+//    split goes to the split-merge kernel.
 #pragma once
 
 #include "tq_common.cuh"
@@ -49,8 +55,7 @@ struct DecodeParams {
   float scale_log2;      // softmax scale * log2(e)
   int chunk;             // tokens per CTA
   int splits;            // CTAs per unit
-  float* part;           // [units*G, splits*(warps per partial), D+2]
-  int* err;              // bounded-wait failure flag (nullable)
+  float* part;           // [units*G, splits*(partials per CTA), D+2]
 };
 
 __device__ __forceinline__ int64_t unit_length(const DecodeParams& p, int64_t u) {
@@ -60,141 +65,224 @@ __device__ __forceinline__ int64_t unit_length(const DecodeParams& p, int64_t u)
   return n < 0 ? 0 : n;
 }
 
-constexpr int kMmaWarps = 8;                  // warps per CTA
-constexpr int kMmaTokensPerCta = kMmaWarps * 16;  // tokens per stage
-constexpr int kMmaStages = 3;                 // ring depth
+constexpr int kMmaWarps = 8;                      // warps per CTA
+constexpr int kMmaTokensPerCta = kMmaWarps * 16;  // chunk granule: one tile per warp
+constexpr float kLazyMaxSlack = 8.f;              // log2 headroom before the max is raised
 
 // ---------------------------------------------------------------------------
-// PTX helpers: mbarrier + bulk copy + mma
+// helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-// Bounded wait on phase `parity`; returns false if it gave up.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t addr = smem_u32(bar);
-  for (uint32_t it = 0; it < (1u << 22); ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
-// Plain (non-multicast) bulk copy global -> own shared memory.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// `n` consecutive bits of a register run starting at static bit `bit`.
-template <int N>
-__device__ __forceinline__ uint32_t run_bits(const uint32_t* r, int bit) {
-  const int w = bit >> 5, s = bit & 31;
-  uint32_t v = (s + N > 32) ? __funnelshift_r(r[w], r[w + 1], s) : (r[w] >> s);
-  return v & ((1u << N) - 1u);
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Load `NB` bits starting at (runtime) bit `start` of a shared-memory word row
-// into registers r[0..], LSB-aligned.  When the run is word-aligned for every
-// lane this is a plain vector of loads.
+// Transpose an 8x8 b16 tile held in mma C-fragment order (lane (r, c) holds
+// row r, cols 2c, 2c+1) so that lane (r, c) holds rows 2c, 2c+1 of column r.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Byte offset of pair-table entry e for this lane, e*128 + lane*4, where e is
+// the NB-bit field at static bit `bit` of the run registers r[].
 template <int NB>
-__device__ __forceinline__ void load_run(uint32_t (&r)[(NB + 31) / 32 + 1], const uint32_t* row,
-                                         int start) {
-  constexpr int NW = (NB + 31) / 32;
-  if ((NB & 31) == 0) {
-    const uint32_t* src = row + (start >> 5);
+__device__ __forceinline__ uint32_t lut_off(const uint32_t* r, int bit, uint32_t lane4) {
+  const int w = bit >> 5, s = bit & 31;
+  constexpr uint32_t M = ((1u << NB) - 1u) << 7;
+  uint32_t v;
+  if (s + NB > 32) v = __funnelshift_r(r[w], r[w + 1], s) << 7;
+  else if (s >= 7) v = r[w] >> (s - 7);
+  else v = r[w] << (7 - s);
+  return (v & M) | lane4;
+}
+
+__device__ __forceinline__ uint32_t lut_ld(const uint32_t* lut, uint32_t byte_off) {
+  return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(lut) + byte_off);
+}
+
+// Raw words of the NB-bit run that starts at bit `start` (< 32) of `row`
+// (W words per token row, global memory).  Word-aligned runs use the widest
+// vector load their alignment allows.  Unaligned runs load the words they
+// touch (never past the row) and are shifted into place by align_run() when
+// they are used, so a prefetch never waits for its own data.
+template <int NB>
+struct Run {
+  static constexpr int NW = (NB + 31) / 32;
+  static constexpr bool ALIGNED = (NB & 31) == 0;
+  static constexpr int RAW = ALIGNED ? NW : NW + 1;
+};
+
+template <int NB, int W>
+__device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const uint32_t* row, int start) {
+  constexpr int NW = Run<NB>::NW;
+  if constexpr (Run<NB>::ALIGNED) {
+    constexpr int VEC = (NW % 4 == 0 && W % 4 == 0) ? 4 : (NW % 2 == 0 && W % 2 == 0) ? 2 : 1;
 #pragma unroll
-    for (int i = 0; i < NW; ++i) r[i] = src[i];
-    r[NW] = 0;
+    for (int i = 0; i < NW; i += VEC) {
+      if constexpr (VEC == 4) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(row + i));
+        raw[i] = v.x; raw[i + 1] = v.y; raw[i + 2] = v.z; raw[i + 3] = v.w;
+      } else if constexpr (VEC == 2) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(row + i));
+        raw[i] = v.x; raw[i + 1] = v.y;
+      } else {
+        raw[i] = __ldg(row + i);
+      }
+    }
   } else {
-    const int w0 = start >> 5, sh = start & 31;
-    uint32_t tmp[NW + 1];
+    const bool tail = start + NB > 32 * NW;  // the run reaches one more word
 #pragma unroll
-    for (int i = 0; i <= NW; ++i) tmp[i] = row[w0 + i];
-#pragma unroll
-    for (int i = 0; i < NW; ++i) r[i] = __funnelshift_r(tmp[i], tmp[i + 1], sh);
-    r[NW] = 0;
+    for (int i = 0; i < NW; ++i) raw[i] = __ldg(row + i);
+    raw[NW] = 0u;
+    if (tail) raw[NW] = __ldg(row + NW);
   }
 }
+
+// Run bits LSB-aligned in r[0..NW-1], r[NW] = 0.
+template <int NB>
+__device__ __forceinline__ void align_run(uint32_t (&r)[Run<NB>::NW + 1], const uint32_t (&raw)[Run<NB>::RAW],
+                                          int start) {
+  constexpr int NW = Run<NB>::NW;
+  if constexpr (Run<NB>::ALIGNED) {
+#pragma unroll
+    for (int i = 0; i < NW; ++i) r[i] = raw[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < NW; ++i) r[i] = __funnelshift_r(raw[i], raw[i + 1], start);
+  }
+  r[NW] = 0;
+}
+
+// Bit j of the interleave mask is set iff (j mod 2b) < b: the low half of a
+// 2b-bit field that starts at a multiple of 2b.
+template <int BITS>
+__host__ __device__ constexpr uint32_t pair_mask(int word) {
+  uint32_t m = 0;
+  for (int t = 0; t < 32; ++t)
+    if (((32 * word + t) % (2 * BITS)) < BITS) m |= 1u << t;
+  return m;
+}
+
+// Interleave the runs of token t (A) and t+1 (B): field k (2b bits at bit
+// 2b*k) of ev = code_t(2k) | code_t+1(2k) << b, of od the same at run
+// position 2k+1.  Funnel shifts carry across words, so fields that straddle a
+// word edge (3-bit) come out whole.  Bits past the run are don't-care.
+template <int BITS, int NR>
+__device__ __forceinline__ void pair_tokens(const uint32_t* A, const uint32_t* B, uint32_t* ev, uint32_t* od) {
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    const uint32_t m = pair_mask<BITS>(i);
+    const uint32_t b_up = i == 0 ? (B[0] << BITS) : __funnelshift_l(B[i - 1], B[i], BITS);
+    const uint32_t a_dn = i + 1 < NR ? __funnelshift_r(A[i], A[i + 1], BITS) : (A[i] >> BITS);
+    ev[i] = (A[i] & m) | (b_up & ~m);
+    od[i] = (a_dn & m) | (B[i] & ~m);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// configuration
+// ---------------------------------------------------------------------------
+template <int D, int BITS, int NT>
+struct MmaCfg {
+  static constexpr int W = D * BITS / 32;     // words per token
+  static constexpr int NP = 1 << (2 * BITS);  // pair-table entries
+  static constexpr int LUT_WORDS = NP * 32;   // per table (one copy per lane)
+  static constexpr int RUNK = D / 4 * BITS;   // K bits per lane
+  static constexpr int RUNV = D / 8 * BITS;   // V bits per lane
+  static constexpr int RK = Run<RUNK>::NW + 1;
+  static constexpr int RV = Run<RUNV>::NW + 1;
+  static constexpr int KB = D / 16;           // k-blocks (score) = m-blocks (value)
+  static constexpr int GM = 8 * NT;           // padded group size
+  static constexpr int FRAG = NT * KB * 4 * 32;  // accumulator words of one warp
+  static constexpr size_t MAIN_BYTES = (size_t)2 * LUT_WORDS * 4 + (size_t)GM * D * 4;
+  static constexpr size_t MERGE_BYTES =
+      ((size_t)kMmaWarps * FRAG + 3 * kMmaWarps * GM + 2 * GM) * 4;
+  static constexpr size_t SMEM_BYTES = MAIN_BYTES > MERGE_BYTES ? MAIN_BYTES : MERGE_BYTES;
+};
+
+// Raw code words of one 16-token tile of a lane.
+template <int D, int BITS>
+struct TileRegs {
+  static constexpr int KR = Run<MmaCfg<D, BITS, 1>::RUNK>::RAW;
+  static constexpr int VR = Run<MmaCfg<D, BITS, 1>::RUNV>::RAW;
+  uint32_t k0[KR], k1[KR];  // token rows r, r+8
+  uint32_t va[VR], vb[VR];  // tokens 2c, 2c+1
+  uint32_t vc[VR], vd[VR];  // tokens 2c+8, 2c+9
+};
+
+// Per-lane load plan, fixed for the whole token loop: the lane reads K token
+// rows r and r+8 at bit offset c*RUNK and V rows 2c, 2c+1, 2c+8, 2c+9 at bit
+// offset r*RUNV of each row.
+struct LanePlan {
+  int k_row, v_row;    // word offsets of the lane's first K / V run within a tile
+  int k_word, v_word;  // word offset of the run inside a token row
+  int k_bit, v_bit;    // bit offset of the run inside its first word
+};
+
+template <int D, int BITS>
+__device__ __forceinline__ void load_tile(TileRegs<D, BITS>& t, const uint32_t* kt, const uint32_t* vt,
+                                          const LanePlan& lp) {
+  using C = MmaCfg<D, BITS, 1>;
+  constexpr int W = C::W;
+  load_raw<C::RUNK, W>(t.k0, kt + lp.k_row, lp.k_bit);
+  load_raw<C::RUNK, W>(t.k1, kt + lp.k_row + 8 * W, lp.k_bit);
+  load_raw<C::RUNV, W>(t.va, vt + lp.v_row, lp.v_bit);
+  load_raw<C::RUNV, W>(t.vb, vt + lp.v_row + W, lp.v_bit);
+  load_raw<C::RUNV, W>(t.vc, vt + lp.v_row + 8 * W, lp.v_bit);
+  load_raw<C::RUNV, W>(t.vd, vt + lp.v_row + 9 * W, lp.v_bit);
+}
+
+// Tile that runs past the unit's last token: rows are clamped to `last`
+// (relative to the tile start) so no load leaves the unit.
+template <int D, int BITS>
+__device__ __forceinline__ void load_tile_clamped(TileRegs<D, BITS>& t, const uint32_t* kt, const uint32_t* vt,
+                                                  int last, int gr, int tq, const LanePlan& lp) {
+  using C = MmaCfg<D, BITS, 1>;
+  constexpr int W = C::W;
+  auto row = [&](int r) { return (r < last ? r : last) * W; };
+  load_raw<C::RUNK, W>(t.k0, kt + row(gr) + lp.k_word, lp.k_bit);
+  load_raw<C::RUNK, W>(t.k1, kt + row(gr + 8) + lp.k_word, lp.k_bit);
+  load_raw<C::RUNV, W>(t.va, vt + row(2 * tq) + lp.v_word, lp.v_bit);
+  load_raw<C::RUNV, W>(t.vb, vt + row(2 * tq + 1) + lp.v_word, lp.v_bit);
+  load_raw<C::RUNV, W>(t.vc, vt + row(2 * tq + 8) + lp.v_word, lp.v_bit);
+  load_raw<C::RUNV, W>(t.vd, vt + row(2 * tq + 9) + lp.v_word, lp.v_bit);
+}
+
+// d = 256 tiles need more registers; smaller heads run two CTAs per SM.
+template <int D>
+constexpr int mma_min_blocks() { return D == 256 ? 1 : 2; }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 template <int D, int BITS, int NT>
-struct MmaCfg {
-  static constexpr int W = D * BITS / 32;               // words per token
-  static constexpr int NP = 1 << (2 * BITS);            // pair-table entries
-  static constexpr int LUT_WORDS = NP * 32;             // per table
-  static constexpr int STAGE_TOK = kMmaTokensPerCta;
-  static constexpr int STAGE_WORDS = STAGE_TOK * W + 4;  // +16 B pad for run over-read
-  static constexpr int RUNK = D / 4 * BITS;             // bits per lane, K
-  static constexpr int RUNV = D / 8 * BITS;             // bits per lane, V
-  static constexpr int KB = D / 16;                     // k-blocks (score) = m-blocks (value)
-  static constexpr int GM = 8 * NT;                     // padded group size
-  static constexpr size_t SMEM_BYTES =
-      (size_t)(2 * LUT_WORDS + 2 * kMmaStages * STAGE_WORDS) * 4 +
-      (size_t)GM * D * 4 /* rotated queries */ + (size_t)kMmaWarps * GM * 16 * 2 /* P tiles */ +
-      kMmaStages * 8 /* mbarriers */ + 64;
-};
-
-template <int D, int BITS, int NT>
-__global__ void __launch_bounds__(kMmaWarps * 32, 1)
+__global__ void __launch_bounds__(kMmaWarps * 32, mma_min_blocks<D>())
 decode_mma_kernel(DecodeParams p) {
   using C = MmaCfg<D, BITS, NT>;
-  constexpr int W = C::W;
   constexpr int E = D / 32;
   constexpr int KB = C::KB;
   constexpr int GM = C::GM;
+  constexpr int PB = 2 * BITS;  // bits of a code pair
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t* lut_k = reinterpret_cast<uint32_t*>(smem);
   uint32_t* lut_v = lut_k + C::LUT_WORDS;
-  uint32_t* ring_k = lut_v + C::LUT_WORDS;                  // [RS][STAGE_WORDS]
-  uint32_t* ring_v = ring_k + kMmaStages * C::STAGE_WORDS;  // [RS][STAGE_WORDS]
-  float* q_s = reinterpret_cast<float*>(ring_v + kMmaStages * C::STAGE_WORDS);         // [GM][D]
-  __half* p_tiles = reinterpret_cast<__half*>(q_s + GM * D);                            // [NW][GM][16]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(p_tiles + kMmaWarps * GM * 16);
+  float* q_s = reinterpret_cast<float*>(lut_v + C::LUT_WORDS);  // [GM][D]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gr = lane >> 2, tq = lane & 3;
@@ -205,53 +293,45 @@ decode_mma_kernel(DecodeParams p) {
   const int64_t n = unit_length(p, u);
   const int64_t c0 = (int64_t)split * p.chunk;
   const int64_t c1 = min(c0 + (int64_t)p.chunk, n);
-  const int nstages = c1 > c0 ? (int)((c1 - c0 + C::STAGE_TOK - 1) / C::STAGE_TOK) : 0;
+  const int64_t per_warp = p.chunk / kMmaWarps;  // multiple of 16
+  const int64_t w0 = c0 + warp * per_warp;
+  const int64_t w1 = min(w0 + per_warp, c1);
   const uint32_t* kbase = p.k_slab + u * p.unit_stride;
   const uint32_t* vbase = p.v_slab + u * p.unit_stride;
 
-  // ---- producer prologue: barriers + first RS stages ----
-  auto issue = [&](int s) {
-    const int slot = s % kMmaStages;
-    const int64_t t0 = c0 + (int64_t)s * C::STAGE_TOK;
-    const int ntok = (int)min((int64_t)C::STAGE_TOK, c1 - t0);
-    const uint32_t bytes = (uint32_t)ntok * W * 4;
-    const uint32_t bulk = bytes & ~15u;
-    uint32_t* dk = ring_k + slot * C::STAGE_WORDS;
-    uint32_t* dv = ring_v + slot * C::STAGE_WORDS;
-    const uint32_t* sk = kbase + t0 * W;
-    const uint32_t* sv = vbase + t0 * W;
-    if (bulk) {
-      mbar_expect_tx(&bars[slot], 2 * bulk);
-      bulk_g2s(dk, sk, bulk, &bars[slot]);
-      bulk_g2s(dv, sv, bulk, &bars[slot]);
-    } else {
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&bars[slot])) : "memory");
-    }
-    if (bytes != bulk) {  // ragged tail (< 16 B) of 24-byte rows: plain copies
-      for (uint32_t w = bulk / 4; w < bytes / 4; ++w) {
-        dk[w] = __ldg(sk + w);
-        dv[w] = __ldg(sv + w);
-      }
-    }
+  // lane load plan and the first tile (in flight while the tables are built)
+  LanePlan lp;
+  lp.k_word = (tq * C::RUNK) >> 5;
+  lp.k_bit = (tq * C::RUNK) & 31;
+  lp.v_word = (gr * C::RUNV) >> 5;
+  lp.v_bit = (gr * C::RUNV) & 31;
+  lp.k_row = gr * C::W + lp.k_word;
+  lp.v_row = 2 * tq * C::W + lp.v_word;
+  auto fetch = [&](TileRegs<D, BITS>& t, int64_t tile0) {
+    const uint32_t* k = kbase + tile0 * C::W;
+    const uint32_t* v = vbase + tile0 * C::W;
+    if (tile0 + 16 <= n) load_tile<D, BITS>(t, k, v, lp);
+    else load_tile_clamped<D, BITS>(t, k, v, (int)(n - 1 - tile0), gr, tq, lp);
   };
-  if (tid == 0) {
-    for (int s = 0; s < kMmaStages; ++s) mbar_init(&bars[s], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int s = 0; s < kMmaStages && s < nstages; ++s) issue(s);
-  }
+  TileRegs<D, BITS> ta, tb;
+  if (w0 < w1) fetch(ta, w0);
 
-  // ---- pair tables (per-lane copies) ----
+  // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
   {
     constexpr int MASK = (1 << BITS) - 1;
-    for (int i = tid; i < C::LUT_WORDS; i += kMmaWarps * 32) {
-      const int e = i >> 5;
-      lut_k[i] = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + (e >> BITS)));
-      lut_v[i] = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + (e >> BITS)));
+    for (int e = tid; e < C::NP; e += kMmaWarps * 32) {
+      const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + (e >> BITS)));
+      const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + (e >> BITS)));
+      uint4* dk = reinterpret_cast<uint4*>(lut_k + e * 32);
+      uint4* dv = reinterpret_cast<uint4*>(lut_v + e * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dk[i] = make_uint4(hk, hk, hk, hk);
+        dv[i] = make_uint4(hv, hv, hv, hv);
+      }
     }
   }
-
-  // ---- query rows: rotate (exact fp32, as the append path), fold the
-  //      softmax scale in base 2, stage in shared memory ----
+  // ---- query rows: rotate (exact fp32), fold the scale in base 2 ----
   for (int g = warp; g < GM; g += kMmaWarps) {
     float v[E];
     if (g < G) {
@@ -268,8 +348,8 @@ decode_mma_kernel(DecodeParams p) {
   }
   __syncthreads();
 
-  // B fragments of the score mma: lane (r, c) holds head r (+8 nt) at the
-  // dims c*D/4 + 4kb + {0,1} and {2,3}, the same permutation as the K runs.
+  // B fragments of the score mma: lane (r, c) holds head r (+8 nt) at dims
+  // c*D/4 + 4kb + {0,1} and {2,3}, the same permutation as the K runs.
   uint32_t qf[NT][KB][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -280,162 +360,118 @@ decode_mma_kernel(DecodeParams p) {
       qf[nt][kb][1] = pack_half2(qr[2], qr[3]);
     }
 
-  // ---- main loop ----
-  float o[NT][KB][4];   // O^T accumulators: m-block kb, n-tile nt
+  float o[NT][KB][4];  // O^T accumulators: m-block kb, n-tile nt
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int kb = 0; kb < KB; ++kb)
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[nt][kb][e] = 0.f;
-  float mrow[NT][2], lrow[NT][2];
+  float mref[NT][2], lrow[NT][2];  // reference max (uniform over the 8 lanes of a head), row sums
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    mrow[nt][0] = mrow[nt][1] = -INFINITY;
+    mref[nt][0] = mref[nt][1] = -INFINITY;
     lrow[nt][0] = lrow[nt][1] = 0.f;
   }
+  const uint32_t lane4 = (uint32_t)lane * 4u;
 
-  const uint32_t lut_k_lane = smem_u32(lut_k) + lane * 4;
-  const uint32_t lut_v_lane = smem_u32(lut_v) + lane * 4;
-  __half* ptile = p_tiles + warp * GM * 16;
-  bool ok = true;
-
-  for (int s = 0; s < nstages; ++s) {
-    const int slot = s % kMmaStages;
-    if (!mbar_wait(&bars[slot], (uint32_t)((s / kMmaStages) & 1))) ok = false;
-    const int64_t tile0 = c0 + (int64_t)s * C::STAGE_TOK + warp * 16;
-    const int valid = (int)max((int64_t)0, min((int64_t)16, c1 - tile0));
-    if (valid > 0 && ok) {
-      const uint32_t* ks = ring_k + slot * C::STAGE_WORDS + warp * 16 * W;
-      const uint32_t* vs = ring_v + slot * C::STAGE_WORDS + warp * 16 * W;
-      // ---------------- scores ----------------
-      float sc[NT][4];
+  auto process = [&](const TileRegs<D, BITS>& t, int valid) {
+    // ---------------- scores S[t, g] (two independent accumulator chains) ----------------
+    float sc[NT][4], sd[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = sd[nt][e] = 0.f;
+    uint32_t k0[C::RK], k1[C::RK];
+    align_run<C::RUNK>(k0, t.k0, lp.k_bit);
+    align_run<C::RUNK>(k1, t.k1, lp.k_bit);
+#pragma unroll
+    for (int kb = 0; kb < KB; ++kb) {
+      const uint32_t a0 = lut_ld(lut_k, lut_off<PB>(k0, (2 * kb) * PB, lane4));
+      const uint32_t a1 = lut_ld(lut_k, lut_off<PB>(k1, (2 * kb) * PB, lane4));
+      const uint32_t a2 = lut_ld(lut_k, lut_off<PB>(k0, (2 * kb + 1) * PB, lane4));
+      const uint32_t a3 = lut_ld(lut_k, lut_off<PB>(k1, (2 * kb + 1) * PB, lane4));
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        if (kb & 1) mma_f16(sd[nt], a0, a1, a2, a3, qf[nt][kb][0], qf[nt][kb][1]);
+        else mma_f16(sc[nt], a0, a1, a2, a3, qf[nt][kb][0], qf[nt][kb][1]);
+      }
+    }
+    // ---------------- online softmax with a lazy reference max ----------------
+    const bool v0 = gr < valid, v1 = gr + 8 < valid;
+    bool raise = false;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        sc[nt][e] += sd[nt][e];
+        const bool v = (e < 2) ? v0 : v1;
+        if (!v) sc[nt][e] = -INFINITY;
+        raise |= sc[nt][e] > mref[nt][e & 1] + kLazyMaxSlack;
+      }
+    if (__any_sync(FULL, raise)) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[nt][e] = 0.f;
-      {
-        uint32_t r0[(C::RUNK + 31) / 32 + 1], r1[(C::RUNK + 31) / 32 + 1];
-        load_run<C::RUNK>(r0, ks + gr * W, tq * C::RUNK);
-        load_run<C::RUNK>(r1, ks + (gr + 8) * W, tq * C::RUNK);
-#pragma unroll
-        for (int kb = 0; kb < KB; ++kb) {
-          const uint32_t pa0 = run_bits<2 * BITS>(r0, (2 * kb) * 2 * BITS);
-          const uint32_t pa1 = run_bits<2 * BITS>(r1, (2 * kb) * 2 * BITS);
-          const uint32_t pa2 = run_bits<2 * BITS>(r0, (2 * kb + 1) * 2 * BITS);
-          const uint32_t pa3 = run_bits<2 * BITS>(r1, (2 * kb + 1) * 2 * BITS);
-          const uint32_t a0 = lds32(lut_k_lane + (pa0 << 7));
-          const uint32_t a1 = lds32(lut_k_lane + (pa1 << 7));
-          const uint32_t a2 = lds32(lut_k_lane + (pa2 << 7));
-          const uint32_t a3 = lds32(lut_k_lane + (pa3 << 7));
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma16816(sc[nt], a0, a1, a2, a3, qf[nt][kb][0], qf[nt][kb][1]);
-        }
-      }
-      // ---------------- online softmax ----------------
-      const bool v0 = gr < valid, v1 = gr + 8 < valid;
-      float alpha[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
         for (int e = 0; e < 2; ++e) {
-          float s0 = v0 ? sc[nt][e] : -INFINITY;
-          float s1 = v1 ? sc[nt][2 + e] : -INFINITY;
-          float tm = fmaxf(s0, s1);
+          float tm = fmaxf(sc[nt][e], sc[nt][2 + e]);
           tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 4));
           tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 8));
           tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 16));
-          const float mn = fmaxf(mrow[nt][e], tm);
-          alpha[nt][e] = exp2f(mrow[nt][e] - mn);
-          mrow[nt][e] = mn;
-          const __half h0 = __float2half_rn(exp2f(s0 - mn));
-          const __half h1 = __float2half_rn(exp2f(s1 - mn));
-          lrow[nt][e] = lrow[nt][e] * alpha[nt][e] + (__half2float(h0) + __half2float(h1));
-          // P^T tile for the value mma: ptile[g][token]
-          ptile[(nt * 8 + 2 * tq + e) * 16 + gr] = h0;
-          ptile[(nt * 8 + 2 * tq + e) * 16 + gr + 8] = h1;
-        }
-      }
+          const float mn = fmaxf(mref[nt][e], tm);
+          const float alpha = fast_exp2(mref[nt][e] - mn);  // -inf -> 0
+          mref[nt][e] = mn;
+          lrow[nt][e] *= alpha;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int kb = 0; kb < KB; ++kb) {
-          o[nt][kb][0] *= alpha[nt][0];
-          o[nt][kb][1] *= alpha[nt][1];
-          o[nt][kb][2] *= alpha[nt][0];
-          o[nt][kb][3] *= alpha[nt][1];
-        }
-      __syncwarp();
-      uint32_t pb[NT][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        pb[nt][0] = *reinterpret_cast<const uint32_t*>(ptile + (nt * 8 + gr) * 16 + 2 * tq);
-        pb[nt][1] = *reinterpret_cast<const uint32_t*>(ptile + (nt * 8 + gr) * 16 + 2 * tq + 8);
-      }
-      // ---------------- values ----------------
-      {
-        constexpr int RW = (C::RUNV + 31) / 32 + 1;
-        uint32_t ra[RW], rb[RW], rc[RW], rd[RW];  // tokens 2tq, 2tq+1, 2tq+8, 2tq+9
-        load_run<C::RUNV>(ra, vs + (2 * tq) * W, gr * C::RUNV);
-        load_run<C::RUNV>(rb, vs + (2 * tq + 1) * W, gr * C::RUNV);
-        load_run<C::RUNV>(rc, vs + (2 * tq + 8) * W, gr * C::RUNV);
-        load_run<C::RUNV>(rd, vs + (2 * tq + 9) * W, gr * C::RUNV);
-        // m-block mb uses run codes 2mb (row gr) and 2mb+1 (row gr+8)
-#pragma unroll
-        for (int mb = 0; mb < KB; ++mb) {
-          uint32_t i0, i1, i2, i3;
-          if constexpr (BITS == 4) {
-            const int wj = (2 * mb) / 8, by = mb % 4;
-            const uint32_t A = ra[wj], B = rb[wj], Cc = rc[wj], Dd = rd[wj];
-            const uint32_t ev01 = (A & 0x0F0F0F0Fu) | ((B << 4) & 0xF0F0F0F0u);
-            const uint32_t od01 = ((A >> 4) & 0x0F0F0F0Fu) | (B & 0xF0F0F0F0u);
-            const uint32_t ev89 = (Cc & 0x0F0F0F0Fu) | ((Dd << 4) & 0xF0F0F0F0u);
-            const uint32_t od89 = ((Cc >> 4) & 0x0F0F0F0Fu) | (Dd & 0xF0F0F0F0u);
-            i0 = (ev01 >> (8 * by)) & 0xFFu;
-            i1 = (od01 >> (8 * by)) & 0xFFu;
-            i2 = (ev89 >> (8 * by)) & 0xFFu;
-            i3 = (od89 >> (8 * by)) & 0xFFu;
-          } else if constexpr (BITS == 2) {
-            const int wj = (2 * mb) / 16, nb = mb % 8;
-            const uint32_t A = ra[wj], B = rb[wj], Cc = rc[wj], Dd = rd[wj];
-            const uint32_t ev01 = (A & 0x33333333u) | ((B << 2) & 0xCCCCCCCCu);
-            const uint32_t od01 = ((A >> 2) & 0x33333333u) | (B & 0xCCCCCCCCu);
-            const uint32_t ev89 = (Cc & 0x33333333u) | ((Dd << 2) & 0xCCCCCCCCu);
-            const uint32_t od89 = ((Cc >> 2) & 0x33333333u) | (Dd & 0xCCCCCCCCu);
-            i0 = (ev01 >> (4 * nb)) & 0xFu;
-            i1 = (od01 >> (4 * nb)) & 0xFu;
-            i2 = (ev89 >> (4 * nb)) & 0xFu;
-            i3 = (od89 >> (4 * nb)) & 0xFu;
-          } else {
-            const int be = (2 * mb) * BITS, bo = (2 * mb + 1) * BITS;
-            i0 = run_bits<BITS>(ra, be) | (run_bits<BITS>(rb, be) << BITS);
-            i1 = run_bits<BITS>(ra, bo) | (run_bits<BITS>(rb, bo) << BITS);
-            i2 = run_bits<BITS>(rc, be) | (run_bits<BITS>(rd, be) << BITS);
-            i3 = run_bits<BITS>(rc, bo) | (run_bits<BITS>(rd, bo) << BITS);
+          for (int kb = 0; kb < KB; ++kb) {
+            o[nt][kb][e] *= alpha;
+            o[nt][kb][2 + e] *= alpha;
           }
-          const uint32_t a0 = lds32(lut_v_lane + (i0 << 7));
-          const uint32_t a1 = lds32(lut_v_lane + (i1 << 7));
-          const uint32_t a2 = lds32(lut_v_lane + (i2 << 7));
-          const uint32_t a3 = lds32(lut_v_lane + (i3 << 7));
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt) mma16816(o[nt][mb], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
         }
-      }
     }
-    __syncthreads();  // every warp is done with this slot
-    if (tid == 0 && s + kMmaStages < nstages) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(s + kMmaStages);
+    uint32_t pb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const __half2 lo = __floats2half2_rn(fast_exp2(sc[nt][0] - mref[nt][0]), fast_exp2(sc[nt][1] - mref[nt][1]));
+      const __half2 hi = __floats2half2_rn(fast_exp2(sc[nt][2] - mref[nt][0]), fast_exp2(sc[nt][3] - mref[nt][1]));
+      const float2 lf = __half22float2(lo), hf = __half22float2(hi);
+      lrow[nt][0] += lf.x + hf.x;
+      lrow[nt][1] += lf.y + hf.y;
+      pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&lo));  // tokens 2c, 2c+1 of head r
+      pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&hi));  // tokens 2c+8, 2c+9
     }
+    // ---------------- values O^T[dim, g] ----------------
+    constexpr int NR = Run<C::RUNV>::NW;
+    uint32_t va[C::RV], vb[C::RV], vc[C::RV], vd[C::RV];
+    align_run<C::RUNV>(va, t.va, lp.v_bit);
+    align_run<C::RUNV>(vb, t.vb, lp.v_bit);
+    align_run<C::RUNV>(vc, t.vc, lp.v_bit);
+    align_run<C::RUNV>(vd, t.vd, lp.v_bit);
+    uint32_t ea[C::RV], oa[C::RV], ec[C::RV], oc[C::RV];
+    pair_tokens<BITS, NR>(va, vb, ea, oa);
+    pair_tokens<BITS, NR>(vc, vd, ec, oc);
+    ea[NR] = oa[NR] = ec[NR] = oc[NR] = 0;
+    // m-block mb: run code 2mb (row r) and 2mb+1 (row r+8) = field mb of ev / od
+#pragma unroll
+    for (int mb = 0; mb < KB; ++mb) {
+      const uint32_t a0 = lut_ld(lut_v, lut_off<PB>(ea, mb * PB, lane4));
+      const uint32_t a1 = lut_ld(lut_v, lut_off<PB>(oa, mb * PB, lane4));
+      const uint32_t a2 = lut_ld(lut_v, lut_off<PB>(ec, mb * PB, lane4));
+      const uint32_t a3 = lut_ld(lut_v, lut_off<PB>(oc, mb * PB, lane4));
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) mma_f16(o[nt][mb], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+    }
+  };
+  // ping-pong: the next tile's loads are issued before the current tile's math
+  for (int64_t t0 = w0; t0 < w1; t0 += 32) {
+    if (t0 + 16 < w1) fetch(tb, t0 + 16);
+    process(ta, (int)min((int64_t)16, w1 - t0));
+    if (t0 + 16 >= w1) break;
+    if (t0 + 32 < w1) fetch(ta, t0 + 32);
+    process(tb, (int)min((int64_t)16, w1 - t0 - 16));
   }
-  if (!ok && p.err && lane == 0) atomicExch(p.err, TQ_E_TIMEOUT);
 
-  // ---- merge the warps of this CTA in shared memory (reuse the ring) ----
-  float* red_o = reinterpret_cast<float*>(ring_k);  // [GM][D]
-  float* red_m = red_o + GM * D;                    // [NW][GM]
-  float* red_l = red_m + kMmaWarps * GM;            // [NW][GM]
-  float* fin_m = red_l + kMmaWarps * GM;            // [GM]
-  // full l per column: reduce lane partials across gr
+  // ---- merge the warps of this CTA through shared memory (reusing the tables) ----
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -446,13 +482,26 @@ decode_mma_kernel(DecodeParams p) {
       lv += __shfl_xor_sync(FULL, lv, 16);
       lrow[nt][e] = lv;
     }
-  for (int i = tid; i < GM * D; i += kMmaWarps * 32) red_o[i] = 0.f;
+  __syncthreads();  // all warps are done with the tables
+  float* frag = reinterpret_cast<float*>(smem);       // [NW][FRAG] accumulators in fragment order
+  float* red_m = frag + kMmaWarps * C::FRAG;          // [NW][GM]
+  float* red_l = red_m + kMmaWarps * GM;              // [NW][GM]
+  float* scale = red_l + kMmaWarps * GM;              // [NW][GM]
+  float* fin_m = scale + kMmaWarps * GM;              // [GM]
+  float* fin_l = fin_m + GM;                          // [GM]
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int mb = 0; mb < KB; ++mb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) frag[warp * C::FRAG + ((nt * KB + mb) * 4 + e) * 32 + lane] = o[nt][mb][e];
   if (gr == 0) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        red_m[warp * GM + nt * 8 + 2 * tq + e] = mrow[nt][e];
+        const bool seen = lrow[nt][e] > 0.f;
+        red_m[warp * GM + nt * 8 + 2 * tq + e] = seen ? mref[nt][e] : -INFINITY;
         red_l[warp * GM + nt * 8 + 2 * tq + e] = lrow[nt][e];
       }
   }
@@ -460,45 +509,39 @@ decode_mma_kernel(DecodeParams p) {
   if (tid < GM) {
     float M = -INFINITY;
     for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, red_m[w * GM + tid]);
-    fin_m[tid] = M;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    float f[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const float M = fin_m[nt * 8 + 2 * tq + e];
-      f[e] = (mrow[nt][e] == -INFINITY) ? 0.f : exp2f(mrow[nt][e] - M);
-    }
-#pragma unroll
-    for (int mb = 0; mb < KB; ++mb) {
-      const int dlo = gr * (D / 8) + 2 * mb;  // row gr; row gr+8 -> dlo + 1
-      const int g0 = nt * 8 + 2 * tq;
-      atomicAdd(&red_o[g0 * D + dlo], o[nt][mb][0] * f[0]);
-      atomicAdd(&red_o[(g0 + 1) * D + dlo], o[nt][mb][1] * f[1]);
-      atomicAdd(&red_o[g0 * D + dlo + 1], o[nt][mb][2] * f[0]);
-      atomicAdd(&red_o[(g0 + 1) * D + dlo + 1], o[nt][mb][3] * f[1]);
-    }
-  }
-  __syncthreads();
-  for (int g = warp; g < G && g < GM; g += kMmaWarps) {
-    const float M = fin_m[g];
-    float Ls = 0.f;
+    float L = 0.f;
     for (int w = 0; w < kMmaWarps; ++w) {
-      const float mw = red_m[w * GM + g];
-      if (mw != -INFINITY) Ls += red_l[w * GM + g] * exp2f(mw - M);
+      const float mw = red_m[w * GM + tid];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      scale[w * GM + tid] = f;
+      L += red_l[w * GM + tid] * f;
     }
-    float* dst = p.part + ((u * G + g) * (int64_t)p.splits + split) * (D + 2);
-    for (int i = lane; i < D; i += 32) dst[i] = red_o[g * D + i];
-    if (lane == 0) {
-      dst[D] = M;
-      dst[D + 1] = Ls;
-    }
+    fin_m[tid] = M;
+    fin_l[tid] = L;
+  }
+  __syncthreads();
+  // element i of a warp's fragment slab = (nt, mb, e, lane) -> (head, dim)
+  for (int i = tid; i < C::FRAG; i += kMmaWarps * 32) {
+    const int ln = i & 31, e = (i >> 5) & 3, blk = i >> 7;
+    const int nt = blk / KB, mb = blk % KB;
+    const int g = nt * 8 + 2 * (ln & 3) + (e & 1);
+    if (g >= G) continue;
+    const int dim = (ln >> 2) * (D / 8) + 2 * mb + (e >> 1);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMmaWarps; ++w) acc = fmaf(frag[w * C::FRAG + i], scale[w * GM + g], acc);
+    p.part[((u * G + g) * (int64_t)p.splits + split) * (D + 2) + dim] = acc;
+  }
+  if (tid < G && tid < GM) {
+    float* dst = p.part + ((u * G + tid) * (int64_t)p.splits + split) * (D + 2);
+    dst[D] = fin_m[tid];
+    dst[D + 1] = fin_l[tid];
   }
 }
 
 // Launches the tensor-core kernel for (D, BITS) (tq_decode_mma.cu).
 void launch_mma_dispatch(int D, int bits, const DecodeParams& p, cudaStream_t st);
+// Resident CTAs per SM of the tensor-core kernel for (D, BITS, G).
+int mma_blocks_per_sm(int D, int bits, int G);
 
 }  // namespace tq

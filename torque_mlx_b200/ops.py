@@ -54,10 +54,11 @@ class Workspace:
 _default_ws = Workspace()
 
 
-def workspace_bytes(units: int, group_size: int, head_dim: int, max_len: int, mode: str | int = "auto") -> int:
+def workspace_bytes(units: int, group_size: int, head_dim: int, bits: int, max_len: int,
+                    mode: str | int = "auto") -> int:
     lib = _lib.load(require_cuda=False)
     out = _lib.c_size_t(0)
-    _lib.check(lib.tq_decode_workspace_size(units, group_size, head_dim, max_len, decode_mode_code(mode),
+    _lib.check(lib.tq_decode_workspace_size(units, group_size, head_dim, bits, max_len, decode_mode_code(mode),
                                             _lib.ctypes.byref(out)), "decode workspace")
     return int(out.value)
 
@@ -70,7 +71,7 @@ def decode_raw(*, query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tenso
                scale: float | None = None, mode: str | int = "auto", workspace: Workspace | None = None) -> None:
     """One ``tq_decode`` call on prepared device tensors (see include/torque_b200.h)."""
     lib = _lib.load()
-    ws = (workspace or _default_ws).get(workspace_bytes(units, group_size, head_dim, max_len, mode), out.device)
+    ws = (workspace or _default_ws).get(workspace_bytes(units, group_size, head_dim, bits, max_len, mode), out.device)
     sl, sr = signs if signs is not None else (None, None)
     _lib.check(lib.tq_decode(
         query.data_ptr(), int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(), v_slab.data_ptr(),
