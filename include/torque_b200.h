@@ -41,7 +41,8 @@ enum tq_status {
   TQ_E_CUDA = -4,      /* a CUDA call failed            -> RuntimeError                      */
   TQ_E_TIMEOUT = -5,   /* a bounded device wait gave up -> RuntimeError                      */
   TQ_E_WORKSPACE = -6, /* workspace missing/too small   -> RuntimeError                      */
-  TQ_E_ARG = -7        /* null pointer / bad enum value -> ValueError                        */
+  TQ_E_ARG = -7,       /* null pointer / bad enum value -> ValueError                        */
+  TQ_E_SCRATCH_LIMIT = -8 /* needs more than the built-in decode scratch -> ValueError        */
 };
 
 enum tq_dtype { TQ_F32 = 0, TQ_F16 = 1, TQ_BF16 = 2 };
@@ -146,6 +147,35 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
               int bits, const float* cent_k, const float* cent_v, float scale, float* out,
               float* lse, int inverse_rotate_output, int mode, void* workspace,
               size_t workspace_bytes, tq_stream_t stream);
+
+/* Allocation-free variant of tq_decode.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory (or must not at this point):
+ * code that runs inside a memory pool or allocator it does not own, a host
+ * language binding with no handle on the CUDA allocator, or a serving loop
+ * whose memory budget is fixed once at start-up.  Same arguments and result as
+ * tq_decode without the workspace pair: the split-K partials go to a scratch
+ * array compiled into the library, TQ_DECODE_STATIC_SCRATCH_BYTES (16 MiB) per
+ * GPU, which every GPU that loads the library holds until the process exits.
+ *  - A decode whose plan needs more scratch than that (tq_decode_workspace_size
+ *    reports the need) returns TQ_E_SCRATCH_LIMIT and launches nothing.
+ *  - The first call on a device looks up that device's copy of the array
+ *    (with the device current); make that first call outside any CUDA stream
+ *    capture.
+ *  - Every call on a device shares the one array.  Calls whose kernels may run
+ *    at the same time on the GPU (different streams without ordering between
+ *    them) race on it and give wrong results; order them on one stream.
+ *  - Nothing in the array needs to start at zero: each call overwrites every
+ *    partial it later reads.
+ *  - It calls no allocator (no cudaMalloc / cudaFree). */
+#define TQ_DECODE_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+int tq_decode_static(const float* query, int rotate_query, const float* signs_left,
+                     const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
+                     int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
+                     int64_t len_offset, int64_t max_len, int64_t units, int group_size,
+                     int head_dim, int bits, const float* cent_k, const float* cent_v, float scale,
+                     float* out, float* lse, int inverse_rotate_output, int mode,
+                     tq_stream_t stream);
 
 /* Merge P normalised partial attentions over disjoint key sets (the sequence
  * shards of a multi-GPU decode):

@@ -25,11 +25,12 @@ TQ_E_CUDA = -4
 TQ_E_TIMEOUT = -5
 TQ_E_WORKSPACE = -6
 TQ_E_ARG = -7
+TQ_E_SCRATCH_LIMIT = -8
 
 TQ_F32, TQ_F16, TQ_BF16 = 0, 1, 2
 DECODE_AUTO, DECODE_EXACT, DECODE_TENSOR = 0, 1, 2
 
-_VALUE_ERRORS = {TQ_E_BITS, TQ_E_HEAD_DIM, TQ_E_SHAPE, TQ_E_ARG}
+_VALUE_ERRORS = {TQ_E_BITS, TQ_E_HEAD_DIM, TQ_E_SHAPE, TQ_E_ARG, TQ_E_SCRATCH_LIMIT}
 
 # name -> (restype, argtypes); must match include/torque_b200.h
 SIGNATURES: dict[str, tuple] = {
@@ -49,6 +50,9 @@ SIGNATURES: dict[str, tuple] = {
     "tq_decode": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
                           c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
                           c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "tq_decode_static": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
+                                 c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
+                                 c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "tq_lse_merge": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p,
                              c_void_p, c_void_p]),
 }

@@ -220,6 +220,7 @@ const char* tq_status_string(int s) {
     case TQ_E_TIMEOUT: return "device wait timed out";
     case TQ_E_WORKSPACE: return "workspace missing or too small";
     case TQ_E_ARG: return "invalid argument";
+    case TQ_E_SCRATCH_LIMIT: return "decode needs more scratch than the library's built-in 16 MiB (use tq_decode with a workspace)";
     default: return "unknown status";
   }
 }

@@ -15,6 +15,7 @@
 #include "tq_decode_mma.cuh"  // DecodeParams, kMma*
 
 #include <math.h>
+#include <mutex>
 
 namespace tq {
 
@@ -440,6 +441,69 @@ int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, 
   else if (head_dim == 128) lse_merge_kernel<128><<<grid, 256, 0, st>>>(outs, lses, parts, rows, out, lse_out, inverse_rotate, signs_left, signs_right);
   else lse_merge_kernel<256><<<grid, 256, 0, st>>>(outs, lses, parts, rows, out, lse_out, inverse_rotate, signs_left, signs_right);
   return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode: the split partials live in a scratch array compiled
+// into this library instead of a caller-provided workspace.
+// ---------------------------------------------------------------------------
+}  // extern "C"
+
+namespace tq {
+
+// One copy per GPU that loads the library, alive until the process exits.
+static __device__ __align__(256) unsigned char g_decode_scratch[TQ_DECODE_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+static void* g_scratch_ptr[kMaxDevices];  // device address of g_decode_scratch, per device
+static std::mutex g_scratch_mutex;
+
+// Device address of this device's scratch.  In host code the array's name is
+// only a host-side stand-in, so the real address is looked up once per device
+// (with that device current) and cached.
+static int scratch_for_current_device(void** ptr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return TQ_E_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return TQ_E_ARG;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || !p) {
+      set_last_cuda_error(e);
+      return TQ_E_CUDA;
+    }
+    g_scratch_ptr[dev] = p;
+  }
+  *ptr = g_scratch_ptr[dev];
+  return TQ_OK;
+}
+
+}  // namespace tq
+
+extern "C" {
+
+int tq_decode_static(const float* query, int rotate_query, const float* signs_left,
+                     const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
+                     int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
+                     int64_t len_offset, int64_t max_len, int64_t units, int group_size,
+                     int head_dim, int bits, const float* cent_k, const float* cent_v, float scale,
+                     float* out, float* lse, int inverse_rotate_output, int mode,
+                     tq_stream_t stream) {
+  size_t need = 0;
+  int s = tq_decode_workspace_size(units, group_size, head_dim, bits, max_len, mode, &need);
+  if (s != TQ_OK) return s;
+  if (need > TQ_DECODE_STATIC_SCRATCH_BYTES) return TQ_E_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  s = scratch_for_current_device(&scratch);
+  if (s != TQ_OK) return s;
+  return tq_decode(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
+                   units_per_seq, len_offset, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale,
+                   out, lse, inverse_rotate_output, mode, scratch, TQ_DECODE_STATIC_SCRATCH_BYTES, stream);
 }
 
 }  // extern "C"
