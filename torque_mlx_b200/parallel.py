@@ -1,0 +1,190 @@
+"""Multi-GPU partitions of the packed-KV decode path (one process per GPU).
+
+The reference runs on one device only; these partitions are new.
+
+* Batch sharding: each rank owns whole sequences and runs
+  the unchanged single-GPU step; there is no collective on the data path.
+  ``shard_batch`` gives the rank's slice.
+
+* Sequence sharding (long batch-1 contexts): each rank
+  owns a contiguous share of the prefill tokens plus the new tokens it is
+  assigned round-robin.  A decode step is
+      local tq_decode over the rank's tokens -> (o_r rotated, lse_r)
+      all-gather of [o_r | lse_r] over the process group (NCCL over NVLink)
+      tq_lse_merge:  o = sum_r exp(lse_r - LSE) o_r  (then Pi^T)
+  which equals attention over the union of the shards.
+
+Everything here that is not a kernel launch (the token plan, packing the
+exchange buffer, the all-gather) is plain torch.distributed and is tested on
+CPU with gloo ranks; the merge itself is ``tq_lse_merge`` on the GPU.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+def shard_batch(batch: int, rank: int, world: int) -> tuple[int, int]:
+    """[start, stop) of the sequences rank ``rank`` owns (contiguous, sizes differ by <= 1)."""
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+@dataclass
+class SequencePlan:
+    """Which rank holds which token positions of one sequence."""
+
+    world: int
+    prefill: int
+
+    def prefill_range(self, rank: int) -> tuple[int, int]:
+        """Contiguous share of the prefill tokens."""
+        return shard_batch(self.prefill, rank, self.world)
+
+    def owner(self, position: int) -> int:
+        """Rank that stores token ``position``: the prefill shards, then round robin."""
+        if position < self.prefill:
+            base, extra = divmod(self.prefill, self.world)
+            big = extra * (base + 1)
+            return position // (base + 1) if position < big else extra + (position - big) // max(base, 1)
+        return (position - self.prefill) % self.world
+
+    def local_count(self, rank: int, length: int) -> int:
+        """Tokens rank holds when the sequence is ``length`` long."""
+        a, b = self.prefill_range(rank)
+        n = b - a
+        extra = max(0, length - self.prefill)
+        n += extra // self.world + (1 if rank < extra % self.world else 0)
+        return n
+
+
+def gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """All-gather every rank's normalised partial ``out [rows, d]`` and its
+    ``lse [rows]``; returns ``([P, rows, d], [P, rows])``.  One collective:
+    the two tensors travel as one ``[rows, d + 1]`` buffer."""
+    world = dist.get_world_size(group)
+    rows, d = out.shape
+    buf = torch.empty((rows, d + 1), dtype=torch.float32, device=out.device)
+    buf[:, :d].copy_(out)
+    buf[:, d].copy_(lse)
+    recv = torch.empty((world, rows, d + 1), dtype=torch.float32, device=out.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(recv, buf, group=group)
+    else:
+        dist.all_gather(list(recv.unbind(0)), buf, group=group)
+    return recv[..., :d], recv[..., d].contiguous()
+
+
+class SequenceShardedDecoder:
+    """Decode one long sequence whose packed tokens are spread over the ranks
+    of ``group``.  ``cache`` is this rank's TorqueKVCache (batch 1) holding its
+    share; it must be built with ``fused_weights=True`` so the local decode
+    returns rotated partials — the inverse rotation runs once, after the merge,
+    when ``rotate_back`` is set."""
+
+    def __init__(self, cache, plan: SequencePlan, group=None, rotate_back: bool = True):
+        if not cache.config.fused_weights:
+            raise ValueError("the local shard cache must use fused_weights=True (rotated partials)")
+        if cache.batch_size != 1:
+            raise ValueError("sequence sharding holds one sequence per cache")
+        self.cache = cache
+        self.plan = plan
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.rotate_back = rotate_back
+        self.length = 0  # global sequence length
+
+    def prefill(self, key, value) -> None:
+        """Append this rank's share ``[layers, kv_heads, T_r, d]`` of the prefill."""
+        self.cache.append(key=key, value=value)
+        self.length = self.plan.prefill
+
+    def append(self, key, value) -> None:
+        """Append the next token; only its owner stores it."""
+        if self.plan.owner(self.length) == self.rank:
+            self.cache.append(key=key, value=value)
+        self.length += 1
+
+    def decode(self, query):
+        """Full-sequence decode: local partial -> all-gather -> LSE merge."""
+        from . import ops
+        q = query if isinstance(query, torch.Tensor) else torch.as_tensor(query)
+        out, lse = self.cache.decode(query=q, return_lse=True)
+        shape = out.shape
+        d = shape[-1]
+        outs, lses = gather_partials(out.reshape(-1, d), lse.reshape(-1), self.group)
+        merged = ops.lse_merge(outs, lses, inverse_rotation=self.cache.rotation if self.rotate_back else None)
+        return merged.reshape(shape)
+
+
+def run_sequence_split_bench(args, wl, rank: int, world: int) -> None:
+    """bench.py's sequence-split mode (config 3 at N > 1): a fixed 131072-token
+    context split over the ranks (strong scaling); each step appends one token
+    on its owner rank and decodes across all ranks."""
+    import json
+
+    import torque_mlx_b200 as T
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    H, Hq, d, bits = wl["kv_heads"], wl["q_heads"], wl["head_dim"], wl["bits"]
+    L = wl["len_lo"]
+    plan = SequencePlan(world=world, prefill=L)
+    a, b = plan.prefill_range(rank)
+    cfg = T.TorqueConfig(bit_width=bits, head_dim=d, num_layers=1, kv_heads=H, rotation_seed=0, fused_weights=True)
+    cache = T.TorqueKVCache(config=cfg, initial_capacity=(b - a) + args.warmup + args.steps + 512)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(wl["seed"] * 7919 + rank)
+    for s in range(a, b, 16384):
+        n = min(16384, b - s)
+        cache.append(key=torch.randn((1, H, n, d), generator=gen, device=dev, dtype=torch.float16),
+                     value=torch.randn((1, H, n, d), generator=gen, device=dev, dtype=torch.float16))
+    dec = SequenceShardedDecoder(cache, plan)
+    dec.length = L
+    ring = 8
+    gen.manual_seed(17)  # identical new tokens / queries on every rank
+    new_k = torch.randn((ring, 1, H, d), generator=gen, device=dev, dtype=torch.float16)
+    new_v = torch.randn((ring, 1, H, d), generator=gen, device=dev, dtype=torch.float16)
+    qs = torch.randn((ring, 1, Hq, d), generator=gen, device=dev, dtype=torch.float32)
+    for i in range(args.warmup):
+        dec.append(new_k[i % ring], new_v[i % ring])
+        dec.decode(qs[i % ring])
+    torch.cuda.synchronize()
+    dist.barrier()
+    stream = torch.cuda.current_stream()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for j in range(args.steps):
+        r = (args.warmup + j) % ring
+        dec.append(new_k[r], new_v[r])
+        dec.decode(qs[r])
+    s1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([s0.elapsed_time(s1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    W = T.packed_words_for_head_dim(d, bits)
+    total_bytes = (L + args.warmup + args.steps // 2) * H * 2 * W * 4
+    if rank == 0:
+        from pathlib import Path
+        peaks = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+        peak, kind = ((float(json.loads(peaks.read_text())["hbm_gbs"]), "measured") if peaks.exists()
+                      else (6650.0, "fallback"))
+        achieved = total_bytes / world / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": "decode tokens/s", "value": 1.0 / (ms / 1e3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": f"u32 packed {bits}-bit codes; fp16 mma",
+            "data": "synthetic (seeded fp16 N(0,1) K/V)",
+            "config": {"workload": args.workload, "desc": wl["desc"], "global_batch": 1,
+                       "parallelism": f"sequence-split x{world} + NCCL all-gather + LSE merge"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_kind": kind,
+                         "note": "per-GPU packed bytes / whole step time (decode + all-gather + merge)"},
+            "gpu_launches": 5 * args.steps,
+        }), flush=True)
+    dist.destroy_process_group()
