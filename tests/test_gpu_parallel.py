@@ -34,7 +34,7 @@ def _worker(rank, world, port, q):
         H, G, d, n, extra = 2, 8, 256, 3000, 5
         keys = rng.standard_normal((H, n + extra, d)).astype(np.float16)
         vals = rng.standard_normal((H, n + extra, d)).astype(np.float16)
-        q = rng.standard_normal((H * G, d)).astype(np.float32)
+        qry = rng.standard_normal((H * G, d)).astype(np.float32)
         plan = SequencePlan(world=world, prefill=n)
         a, b = plan.prefill_range(rank)
         cfg = T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H, fused_weights=True)
@@ -42,10 +42,10 @@ def _worker(rank, world, port, q):
         dec.prefill(keys[:, a:b], vals[:, a:b])
         for t in range(n, n + extra):
             dec.append(keys[:, t], vals[:, t])
-        got = dec.decode(torch.from_numpy(q).cuda()).cpu().numpy()
+        got = dec.decode(torch.from_numpy(qry).cuda()).cpu().numpy()
         full = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H))
         full.append(key=keys, value=vals)
-        ref = full.decode(query=q)
+        ref = full.decode(query=qry)
         q.put((rank, float(np.max(np.abs(got - ref)))))
     finally:
         dist.destroy_process_group()
