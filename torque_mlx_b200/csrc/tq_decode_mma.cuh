@@ -9,9 +9,9 @@
 //    while the current one is computed (two register sets, ping-pong).
 //  * A code pair (two b-bit indices) becomes a half2 of centroids with ONE
 //    32-bit shared-memory load from a pair table: entry e holds
-//    (c[e & (2^b-1)], c[e >> b]).  Every lane owns a private copy of the table
-//    in its own bank (entry e of lane l at word e*32 + l), so lookups never
-//    conflict whatever the codes are.
+//    (c[e & (2^b-1)], c[e >> b]).  Every lane owns a private copy of the K and
+//    V tables in its own bank (see lut_off), so lookups never conflict
+//    whatever the codes are.
 //  * scores  S[t, g] = K[t, :] . Qs[g, :]  as M = 16 tokens, N = 8 heads,
 //    K = 16 dims per mma.  Lane (r = lane/4, c = lane%4) takes the contiguous
 //    run of d/4 dims [c*d/4, (c+1)*d/4) of its two token rows, so every code
@@ -99,18 +99,32 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return y;
 }
 
-// Byte offset of pair-table entry e for this lane, e*128 + lane*4, where e is
-// the NB-bit field at static bit `bit` of the run registers r[].
+// Pair tables: K and V entries interleave with a 256-byte stride per entry,
+// K entry e of lane l at byte e*256 + 4l and V entry e at byte e*256 + 128 + 4l,
+// so one offset serves both tables and every lane reads its own bank.
+//
+// Byte offset e*256 + 4*lane of the NB-bit field e at static bit `bit` of the
+// run registers r[].  Byte-aligned 8-bit fields (4-bit codes) take a single
+// byte permute that also inserts the lane term; other fields shift the field
+// to bit 8 and mask, with the lane term ORed in by the same logic op.
 template <int NB>
 __device__ __forceinline__ uint32_t lut_off(const uint32_t* r, int bit, uint32_t lane4) {
   const int w = bit >> 5, s = bit & 31;
-  constexpr uint32_t M = ((1u << NB) - 1u) << 7;
+  if constexpr (NB == 8) {
+    if ((s & 7) == 0) {
+      // result bytes: [lane4, field byte, 0, 0]; selector nibbles index bytes of {r[w], lane4}
+      return __byte_perm(r[w], lane4, 0x5504u | ((uint32_t)(s >> 3) << 4));
+    }
+  }
+  constexpr uint32_t M = ((1u << NB) - 1u) << 8;
   uint32_t v;
-  if (s + NB > 32) v = __funnelshift_r(r[w], r[w + 1], s) << 7;
-  else if (s >= 7) v = r[w] >> (s - 7);
-  else v = r[w] << (7 - s);
+  if (s + NB > 32) v = __funnelshift_r(r[w], r[w + 1], s) << 8;
+  else if (s >= 8) v = r[w] >> (s - 8);
+  else v = r[w] << (8 - s);
   return (v & M) | lane4;
 }
+
+constexpr uint32_t kLutVOffset = 128;  // V entry follows the K entry inside a 256-byte row
 
 __device__ __forceinline__ uint32_t lut_ld(const uint32_t* lut, uint32_t byte_off) {
   return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(lut) + byte_off);
@@ -202,7 +216,7 @@ template <int D, int BITS, int NT>
 struct MmaCfg {
   static constexpr int W = D * BITS / 32;     // words per token
   static constexpr int NP = 1 << (2 * BITS);  // pair-table entries
-  static constexpr int LUT_WORDS = NP * 32;   // per table (one copy per lane)
+  static constexpr int LUT_WORDS = NP * 64;   // K + V tables, 256 B per entry (one copy per lane each)
   static constexpr int RUNK = D / 4 * BITS;   // K bits per lane
   static constexpr int RUNV = D / 8 * BITS;   // V bits per lane
   static constexpr int RK = Run<RUNK>::NW + 1;
@@ -210,7 +224,7 @@ struct MmaCfg {
   static constexpr int KB = D / 16;           // k-blocks (score) = m-blocks (value)
   static constexpr int GM = 8 * NT;           // padded group size
   static constexpr int FRAG = NT * KB * 4 * 32;  // accumulator words of one warp
-  static constexpr size_t MAIN_BYTES = (size_t)2 * LUT_WORDS * 4 + (size_t)GM * D * 4;
+  static constexpr size_t MAIN_BYTES = (size_t)LUT_WORDS * 4 + (size_t)GM * D * 4;
   static constexpr size_t MERGE_BYTES =
       ((size_t)kMmaWarps * FRAG + 3 * kMmaWarps * GM + 2 * GM) * 4;
   static constexpr size_t SMEM_BYTES = MAIN_BYTES > MERGE_BYTES ? MAIN_BYTES : MERGE_BYTES;
@@ -264,9 +278,12 @@ __device__ __forceinline__ void load_tile_clamped(TileRegs<D, BITS>& t, const ui
   load_raw<C::RUNV, W>(t.vd, vt + row(2 * tq + 9) + lp.v_word, lp.v_bit);
 }
 
-// d = 256 tiles need more registers; smaller heads run two CTAs per SM.
+// d = 256 tiles need more registers; smaller heads run TQ_MINB CTAs per SM.
+#ifndef TQ_MINB
+#define TQ_MINB 2
+#endif
 template <int D>
-constexpr int mma_min_blocks() { return D == 256 ? 1 : 2; }
+constexpr int mma_min_blocks() { return D == 256 ? 1 : TQ_MINB; }
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -280,9 +297,8 @@ decode_mma_kernel(DecodeParams p) {
   constexpr int GM = C::GM;
   constexpr int PB = 2 * BITS;  // bits of a code pair
   extern __shared__ __align__(128) uint8_t smem[];
-  uint32_t* lut_k = reinterpret_cast<uint32_t*>(smem);
-  uint32_t* lut_v = lut_k + C::LUT_WORDS;
-  float* q_s = reinterpret_cast<float*>(lut_v + C::LUT_WORDS);  // [GM][D]
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);      // interleaved K/V pair tables
+  float* q_s = reinterpret_cast<float*>(lut + C::LUT_WORDS);  // [GM][D]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gr = lane >> 2, tq = lane & 3;
@@ -322,8 +338,8 @@ decode_mma_kernel(DecodeParams p) {
     for (int e = tid; e < C::NP; e += kMmaWarps * 32) {
       const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + (e >> BITS)));
       const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + (e >> BITS)));
-      uint4* dk = reinterpret_cast<uint4*>(lut_k + e * 32);
-      uint4* dv = reinterpret_cast<uint4*>(lut_v + e * 32);
+      uint4* dk = reinterpret_cast<uint4*>(lut + e * 64);
+      uint4* dv = reinterpret_cast<uint4*>(lut + e * 64 + 32);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         dk[i] = make_uint4(hk, hk, hk, hk);
@@ -387,10 +403,10 @@ decode_mma_kernel(DecodeParams p) {
     align_run<C::RUNK>(k1, t.k1, lp.k_bit);
 #pragma unroll
     for (int kb = 0; kb < KB; ++kb) {
-      const uint32_t a0 = lut_ld(lut_k, lut_off<PB>(k0, (2 * kb) * PB, lane4));
-      const uint32_t a1 = lut_ld(lut_k, lut_off<PB>(k1, (2 * kb) * PB, lane4));
-      const uint32_t a2 = lut_ld(lut_k, lut_off<PB>(k0, (2 * kb + 1) * PB, lane4));
-      const uint32_t a3 = lut_ld(lut_k, lut_off<PB>(k1, (2 * kb + 1) * PB, lane4));
+      const uint32_t a0 = lut_ld(lut, lut_off<PB>(k0, (2 * kb) * PB, lane4));
+      const uint32_t a1 = lut_ld(lut, lut_off<PB>(k1, (2 * kb) * PB, lane4));
+      const uint32_t a2 = lut_ld(lut, lut_off<PB>(k0, (2 * kb + 1) * PB, lane4));
+      const uint32_t a3 = lut_ld(lut, lut_off<PB>(k1, (2 * kb + 1) * PB, lane4));
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         if (kb & 1) mma_f16(sd[nt], a0, a1, a2, a3, qf[nt][kb][0], qf[nt][kb][1]);
@@ -454,10 +470,10 @@ decode_mma_kernel(DecodeParams p) {
     // m-block mb: run code 2mb (row r) and 2mb+1 (row r+8) = field mb of ev / od
 #pragma unroll
     for (int mb = 0; mb < KB; ++mb) {
-      const uint32_t a0 = lut_ld(lut_v, lut_off<PB>(ea, mb * PB, lane4));
-      const uint32_t a1 = lut_ld(lut_v, lut_off<PB>(oa, mb * PB, lane4));
-      const uint32_t a2 = lut_ld(lut_v, lut_off<PB>(ec, mb * PB, lane4));
-      const uint32_t a3 = lut_ld(lut_v, lut_off<PB>(oc, mb * PB, lane4));
+      const uint32_t a0 = lut_ld(lut, lut_off<PB>(ea, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a1 = lut_ld(lut, lut_off<PB>(oa, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a2 = lut_ld(lut, lut_off<PB>(ec, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a3 = lut_ld(lut, lut_off<PB>(oc, mb * PB, lane4) + kLutVOffset);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma_f16(o[nt][mb], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
     }
