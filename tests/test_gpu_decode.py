@@ -287,3 +287,28 @@ def test_capacity_growth_preserves_codes():
                                                              cache.key_codebook.centroids, 2))
     cache.reset()
     assert cache.sequence_length == 0
+
+
+@pytest.mark.parametrize("mode", ["exact", "tensor"])
+def test_captured_step_matches_eager_steps(mode):
+    """CUDA-graph replay of append + decode equals the eager calls, step after step."""
+    rng = np.random.default_rng(77)
+    cfg = T.TorqueConfig(bit_width=3, head_dim=128, num_layers=1, kv_heads=2)
+    eager = T.TorqueKVCache(config=cfg, batch_size=2, decode_mode=mode, initial_capacity=1024)
+    graph = T.TorqueKVCache(config=cfg, batch_size=2, decode_mode=mode, initial_capacity=1024)
+    for s, n in enumerate((500, 77)):
+        k = rng.standard_normal((1, 2, n, 128)).astype(np.float16)
+        v = rng.standard_normal((1, 2, n, 128)).astype(np.float16)
+        eager.append_sequence(s, key=k, value=v)
+        graph.append_sequence(s, key=k, value=v)
+    nk = torch.from_numpy(rng.standard_normal((2, 1, 2, 128)).astype(np.float16)).cuda()
+    nv = torch.from_numpy(rng.standard_normal((2, 1, 2, 128)).astype(np.float16)).cuda()
+    q = torch.from_numpy(rng.standard_normal((2, 1, 8, 128)).astype(np.float32)).cuda()
+    step = graph.capture_step(key=nk, value=nv, query=q)
+    for _ in range(3):
+        eager.append(key=nk, value=nv)
+        want = eager.decode(query=q)
+        got = step.step().clone()
+        np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), atol=1e-6, rtol=1e-6)
+    assert list(graph.lengths) == list(eager.lengths) == [503, 80]
+    np.testing.assert_array_equal(graph.packed_words()[0], eager.packed_words()[0])

@@ -290,6 +290,10 @@ class TorqueKVCache:
                        "lengths")
             self._len_host[seq] += T
 
+    def _advance_device(self, T: int) -> None:
+        lib = _lib.load()
+        _lib.check(lib.tq_lengths_add(self._len_dev.data_ptr(), self.batch_size, T, _lib.stream_ptr()), "lengths")
+
     def append(self, *, key, value) -> None:
         """Append one step (``[layers, kv_heads, d]`` and the reference's short
         forms) or T tokens (``[layers, kv_heads, T, d]``) to every sequence
@@ -321,15 +325,20 @@ class TorqueKVCache:
             self._advance(T, seq)
 
     # ----------------------------------------------------------------- decode
-    def _decode(self, q: torch.Tensor, hq: int, *, extra: int, return_lse: bool):
+    def _decode(self, q: torch.Tensor, hq: int, *, extra: int, return_lse: bool, full_capacity: bool = False,
+                out: torch.Tensor | None = None):
         cfg = self.config
         G = hq // cfg.kv_heads
         units = self.batch_size * cfg.num_layers * cfg.kv_heads
-        out = torch.empty_like(q)
+        if out is None:
+            out = torch.empty_like(q)
         lse = torch.empty((q.shape[0],), dtype=torch.float32, device=q.device) if return_lse else None
+        # The split plan follows max_len; a captured step plans for the whole
+        # capacity so the graph stays valid while the device lengths grow.
+        max_len = self._cap if full_capacity else min(self._cap, self.sequence_length + extra)
         ops.decode_raw(query=q, k_slab=self._k, v_slab=self._v, unit_stride=self._cap * self._W,
                        lengths=self._len_dev, units_per_seq=cfg.num_layers * cfg.kv_heads, len_offset=extra,
-                       max_len=min(self._cap, self.sequence_length + extra), units=units, group_size=G,
+                       max_len=max_len, units=units, group_size=G,
                        head_dim=cfg.head_dim, bits=cfg.bit_width, cent_k=self._ck, cent_v=self._cv, out=out, lse=lse,
                        rotate_query=self.rotate_queries_on_decode, inverse_rotate=not cfg.fused_weights,
                        signs=self._signs, scale=1.0 / sqrt(cfg.head_dim), mode=self.decode_mode, workspace=self._ws)
@@ -369,6 +378,14 @@ class TorqueKVCache:
 
     decode_mlx_with_current = decode_with_current
 
+    # ------------------------------------------------------------ CUDA graph
+    def capture_step(self, *, key, value, query) -> "CapturedDecodeStep":
+        """Capture one decode step (append one token to every sequence, then
+        attend) into CUDA graphs for launch-free replay.  ``key``/``value``/
+        ``query`` are example CUDA tensors in the shapes ``append``/``decode``
+        take; their contents are copied into static input buffers."""
+        return CapturedDecodeStep(self, key=key, value=value, query=query)
+
     # ------------------------------------------------------------------ misc
     def export_dequantized(self) -> tuple[np.ndarray, np.ndarray]:
         """Dequantized rotated contents ``[layers, kv_heads, seq, d]`` (or with
@@ -404,3 +421,62 @@ class TorqueKVCache:
 # MLX-named alias for drop-in use of the grouped-query cache surface.
 TorqueKVCacheMLX = TorqueKVCache
 TorqueKVCacheB200 = TorqueKVCache
+
+
+class CapturedDecodeStep:
+    """One decode step of a TorqueKVCache replayed from CUDA graphs.
+
+    Two graphs: ``append`` (tq_append_kv + tq_lengths_add on the static key /
+    value buffers) and ``decode`` (tq_decode on the static query buffer into the
+    static output).  The decode plan covers the cache's whole capacity, so the
+    captured launch stays valid as the device lengths grow; call ``step`` (or
+    the two replays) until ``remaining`` reaches zero, then capture again.
+    """
+
+    def __init__(self, cache: TorqueKVCache, *, key, value, query):
+        if not (isinstance(key, torch.Tensor) and key.is_cuda and isinstance(query, torch.Tensor) and query.is_cuda):
+            raise ValueError("capture_step needs CUDA tensors")
+        self.cache = cache
+        k = cache._norm_kv(key, "key")
+        if k.shape[3] != 1:
+            raise ValueError("a captured step appends exactly one token per sequence")
+        self.key = k.clone()
+        self.value = cache._norm_kv(value, "value").to(k.dtype).clone()
+        q, hq, self._out_shape = cache._norm_query(query)
+        self.query = q.clone()
+        self.out = torch.empty_like(self.query)
+        self._hq = hq
+        cache._ensure_capacity(cache.sequence_length + 1)
+        stream = torch.cuda.Stream(device=cache._dev)
+        stream.wait_stream(torch.cuda.current_stream(cache._dev))
+        with torch.cuda.stream(stream):
+            # size the workspace for the capacity plan before capturing
+            cache._decode(self.query, hq, extra=0, return_lse=False, full_capacity=True, out=self.out)
+            stream.synchronize()
+            self.g_append = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_append, stream=stream):
+                cache._write(self.key, self.value)
+                cache._advance_device(1)
+            self.g_decode = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_decode, stream=stream):
+                cache._decode(self.query, hq, extra=0, return_lse=False, full_capacity=True, out=self.out)
+        torch.cuda.current_stream(cache._dev).wait_stream(stream)
+
+    @property
+    def remaining(self) -> int:
+        """Steps left before the captured plan would run past the capacity."""
+        return self.cache.capacity - int(self.cache._len_host.max())
+
+    def append(self) -> None:
+        if self.remaining < 1:
+            raise RuntimeError("cache capacity reached: capture the step again")
+        self.g_append.replay()
+        self.cache._len_host += 1
+
+    def decode(self) -> torch.Tensor:
+        self.g_decode.replay()
+        return self.out.reshape(self._out_shape)
+
+    def step(self) -> torch.Tensor:
+        self.append()
+        return self.decode()
