@@ -162,6 +162,7 @@ decode_exact_kernel(DecodeParams p) {
 // parallel instead of one warp walking every part.
 // ---------------------------------------------------------------------------
 constexpr int kMergeWarps = 8;
+constexpr int kMergeMaxParts = 1024;  // parts weighed in shared memory per pass
 
 template <int D>
 __global__ void __launch_bounds__(kMergeWarps * 32)
@@ -169,56 +170,78 @@ merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
                       float* __restrict__ out, float* __restrict__ lse, int inverse_rotate,
                       const float* __restrict__ signs_left, const float* __restrict__ signs_right) {
   constexpr int E = D / 32;
-  __shared__ float red[kMergeWarps][D];
-  __shared__ float red_l[kMergeWarps];
-  __shared__ float sM;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int T = kMergeWarps * 32;
+  constexpr int SLICES = T / D;  // threads per output dim (parts split between them)
+  __shared__ float w_s[kMergeMaxParts];
+  __shared__ float acc_s[SLICES][D];
+  __shared__ float red[kMergeWarps];
+  __shared__ float sM, sL;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t row = blockIdx.x;
   const float* base = part + row * nparts * (int64_t)(D + 2);
-  float M = -INFINITY;  // max over parts that saw tokens
-  for (int i = threadIdx.x; i < nparts; i += kMergeWarps * 32) {
+  const int np = nparts < kMergeMaxParts ? nparts : kMergeMaxParts;
+
+  // 1) max over parts that saw tokens (m is in log2 units)
+  float M = -INFINITY;
+  for (int i = tid; i < np; i += T) {
     const float* pp = base + i * (int64_t)(D + 2);
     if (pp[D + 1] > 0.f) M = fmaxf(M, pp[D]);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
-  if (lane == 0) red_l[warp] = M;
+  if (lane == 0) red[warp] = M;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     float m = -INFINITY;
-    for (int w = 0; w < kMergeWarps; ++w) m = fmaxf(m, red_l[w]);
+    for (int w = 0; w < kMergeWarps; ++w) m = fmaxf(m, red[w]);
     sM = m;
   }
   __syncthreads();
   M = sM;
-  float v[E];
+  // 2) per-part weights 2^(m_i - M) (0 for empty parts) and the denominator
+  float L = 0.f;
+  for (int i = tid; i < np; i += T) {
+    const float* pp = base + i * (int64_t)(D + 2);
+    const float li = pp[D + 1];
+    const float w = (li > 0.f && M != -INFINITY) ? exp2f(pp[D] - M) : 0.f;
+    w_s[i] = w;
+    L += li * w;
+  }
 #pragma unroll
-  for (int j = 0; j < E; ++j) v[j] = 0.f;
-  float Lw = 0.f;
-  if (M != -INFINITY) {
-    for (int i = warp; i < nparts; i += kMergeWarps) {
-      const float* pp = base + i * (int64_t)(D + 2);
-      const float li = pp[D + 1];
-      if (!(li > 0.f)) continue;
-      const float w = exp2f(pp[D] - M);
-      Lw += li * w;
-#pragma unroll
-      for (int j = 0; j < E; ++j) v[j] = fmaf(pp[j * 32 + lane], w, v[j]);
+  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  if (tid == 0) {
+    float l = 0.f;
+    for (int w = 0; w < kMergeWarps; ++w) l += red[w];
+    sL = l;
+  }
+  // 3) weighted sum: thread (slice, dim) sums parts slice, slice + SLICES, ...
+  //    with independent loads, four in flight
+  {
+    const int dim = tid % D, slice = tid / D;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int i = slice;
+    for (; i + 3 * SLICES < np; i += 4 * SLICES) {
+      a0 = fmaf(base[(int64_t)i * (D + 2) + dim], w_s[i], a0);
+      a1 = fmaf(base[(int64_t)(i + SLICES) * (D + 2) + dim], w_s[i + SLICES], a1);
+      a2 = fmaf(base[(int64_t)(i + 2 * SLICES) * (D + 2) + dim], w_s[i + 2 * SLICES], a2);
+      a3 = fmaf(base[(int64_t)(i + 3 * SLICES) * (D + 2) + dim], w_s[i + 3 * SLICES], a3);
     }
+    for (; i < np; i += SLICES) a0 = fmaf(base[(int64_t)i * (D + 2) + dim], w_s[i], a0);
+    acc_s[slice][dim] = (a0 + a1) + (a2 + a3);
   }
   __syncthreads();
-#pragma unroll
-  for (int j = 0; j < E; ++j) red[warp][j * 32 + lane] = v[j];
-  if (lane == 0) red_l[warp] = Lw;
-  __syncthreads();
   if (warp != 0) return;
-  float Lsum = 0.f;
-  for (int w = 0; w < kMergeWarps; ++w) Lsum += red_l[w];
+  const float Lsum = sL;
+  float v[E];
 #pragma unroll
   for (int j = 0; j < E; ++j) {
-    float acc = 0.f;
-    for (int w = 0; w < kMergeWarps; ++w) acc += red[w][j * 32 + lane];
-    v[j] = M == -INFINITY ? 0.f : acc / Lsum;
+    float a = 0.f;
+#pragma unroll
+    for (int sl = 0; sl < SLICES; ++sl) a += acc_s[sl][j * 32 + lane];
+    v[j] = M == -INFINITY ? 0.f : a / Lsum;
   }
   if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
 #pragma unroll
@@ -309,6 +332,7 @@ static Plan make_plan(int64_t units, int G, int D, int bits, int64_t max_len, in
   int64_t splits = uu < wave ? (wave + uu - 1) / uu : (4 * wave + uu - 1) / uu;
   const int64_t max_splits = (len + tile - 1) / tile;
   if (splits > max_splits) splits = max_splits;
+  if (splits * pl.warps > kMergeMaxParts) splits = kMergeMaxParts / pl.warps;  // merge weighs parts in smem
   if (splits < 1) splits = 1;
   int64_t chunk = (len + splits - 1) / splits;
   chunk = (chunk + tile - 1) / tile * tile;
