@@ -169,6 +169,19 @@ def main() -> None:
     out["sad_q"], out["sad_k"], out["sad_v"] = q, Kp, Vp
     out["sad_out"] = R.streaming_attention_decode(q, Kp, Vp)
 
+    # --- an artifact written by the reference itself (artifact.py:164-184, 246-296)
+    import torque_mlx.artifact as A
+    rng = np.random.default_rng(44)
+    w = {k: rng.standard_normal(s).astype(np.float32) * 0.05
+         for k, s in (("w_q", (64, 32)), ("w_k", (64, 32)), ("w_v", (64, 32)), ("w_o", (48, 64)))}
+    art = A.build_torque_artifact(model_name="tiny", architecture="toy", source_format="npz",
+                                  config=config_mod.TorqueConfig(bit_width=3, head_dim=64, num_layers=2,
+                                                                 kv_heads=2, rotation_seed=9), **w)
+    art_dir = HERE / "artifact_ref"
+    art.save(art_dir, force=True)
+    for k, v in w.items():
+        out[f"artifact_src_{k}"] = v
+
     np.savez_compressed(HERE / "golden.npz", **out)
     total = sum(v.nbytes for v in out.values())
     print(f"wrote {len(out)} arrays, {total / 1e6:.2f} MB raw -> {HERE / 'golden.npz'}")

@@ -49,3 +49,14 @@ __all__ = [
     "packed_words_for_head_dim", "quantize", "quantize_and_pack_rows", "quantize_and_pack_rows_dual",
     "save_codebook", "unpack_indices", "validate_head_dim",
 ]
+from .artifact import (  # noqa: E402
+    TorqueArtifact,
+    TorqueArtifactManifest,
+    build_torque_artifact,
+    convert_npz_checkpoint,
+    load_torque_artifact,
+)
+from .conversion import FusedAttentionWeights, fuse_attention_weights  # noqa: E402
+
+__all__ += ["FusedAttentionWeights", "TorqueArtifact", "TorqueArtifactManifest", "build_torque_artifact",
+            "convert_npz_checkpoint", "fuse_attention_weights", "load_torque_artifact"]
