@@ -42,6 +42,11 @@ WORKLOADS = {
     "config3": dict(batch=1, q_heads=16, kv_heads=2, head_dim=256, bits=4, len_lo=131072, len_hi=131072, seed=3,
                     steps=5000,
                     desc="BASELINE config 3: long-context batch-1 decode, 131072 tokens, 16q/2kv heads, d256, 4-bit"),
+    "config5": dict(batch=1, q_heads=16, kv_heads=8, head_dim=128, bits=4, len_lo=972, len_hi=972, seed=5,
+                    steps=64, layers=28, hidden=2048, ffn=6144, vocab=151936,
+                    desc="BASELINE config 5: random-init 28-layer GQA decoder (hidden 2048, 16q/8kv, d128, FFN 6144, "
+                         "vocab 151936, bf16 N(0,0.02)), 4-bit packed KV with Pi folded into Wq/Wk/Wv/Wo; prefill 972 "
+                         "random tokens, then generate"),
     "longctx128": dict(batch=1, q_heads=32, kv_heads=8, head_dim=128, bits=4, len_lo=131072, len_hi=131072, seed=5,
                        steps=5000,
                        desc="north-star case: batch-1 decode, 131072 tokens, 32q/8kv heads, d128, 4-bit"),
@@ -209,6 +214,55 @@ def build_cache(wl: dict, rank: int, torch, T, extra: int = 256):
     return cache, lens
 
 
+def run_decoder(args, wl) -> None:
+    """Config 5: greedy generation with the whole token step in one CUDA graph."""
+    import torch
+
+    from torque_mlx_b200.decoder import DecoderConfig, PackedKVDecoder
+
+    torch.cuda.set_device(0)
+    cfg = DecoderConfig(num_layers=wl["layers"], hidden=wl["hidden"], q_heads=wl["q_heads"], kv_heads=wl["kv_heads"],
+                        head_dim=wl["head_dim"], ffn=wl["ffn"], vocab=wl["vocab"], bits=wl["bits"], fold="full")
+    model = PackedKVDecoder(cfg, max_tokens=wl["len_lo"] + args.warmup + 2 * args.steps + 64)
+    prompt = torch.randint(0, cfg.vocab, (wl["len_lo"],), generator=torch.Generator().manual_seed(wl["seed"]))
+    tok = model.prefill(prompt.cuda()).argmax(-1).reshape(())
+    model.capture()
+    for _ in range(args.warmup):
+        tok = model.step_graph(tok).clone()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    with ClockSampler(0) as clocks:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            tok = model.step_graph(tok)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    # end to end: eager public API, generated token read back to the host every step
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ids = []
+    for _ in range(min(args.steps, 16)):
+        tok = model.step(tok).argmax(-1).reshape(())
+        ids.append(int(tok.item()))
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / len(ids)
+    weight_bytes = sum(t.numel() * t.element_size() for lay in model.layers for t in lay.values()) + \
+        model.lm_head.numel() * 2
+    peak, kind = _peaks()
+    print(json.dumps({
+        "metric": "decode tokens/s", "value": 1e3 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 weights; u32 packed 4-bit KV", "data": "synthetic (random-init weights, random prompt tokens)",
+        "config": {"workload": "config5", "desc": wl["desc"], "global_batch": 1, "prompt": wl["len_lo"],
+                   "parallelism": "single GPU", "timing": "one CUDA graph per generated token"},
+        "roofline": {"bound": "hbm", "achieved": weight_bytes / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": weight_bytes / (ms / 1e3) / 1e9 / peak, "traffic": None, "peak_kind": kind,
+                     "note": "bf16 weight stream per token (packed KV is ~29 MB of it)"},
+        "e2e": {"value": 1e3 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
+        "gpu_launches": None, "clocks": clocks.summary()}), flush=True)
+
+
 def run_ours(args, wl) -> None:
     import torch
     import torch.distributed as dist
@@ -351,6 +405,8 @@ def main() -> None:
         args.steps = wl["steps"] if args.impl == "ours" else 5
     if args.impl == "reference":
         run_reference(args, wl)
+    elif args.workload == "config5":
+        run_decoder(args, wl)
     else:
         run_ours(args, wl)
 

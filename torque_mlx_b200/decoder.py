@@ -152,8 +152,10 @@ class PackedKVDecoder:
     def _step_body(self, token: torch.Tensor, captured: bool) -> torch.Tensor:
         cfg = self.cfg
         H, Hkv, d = cfg.q_heads, cfg.kv_heads, cfg.head_dim
-        x = self.embed[token.reshape(1)]
-        cos, sin = self.cos[self.pos].reshape(1, -1), self.sin[self.pos].reshape(1, -1)
+        # index_select keeps the lookups on the device (graph-safe, no host sync)
+        x = torch.index_select(self.embed, 0, token.reshape(1))
+        p = self.pos.reshape(1)
+        cos, sin = torch.index_select(self.cos, 0, p), torch.index_select(self.sin, 0, p)
         for lay, cache in zip(self.layers, self.caches):
             h = self._rms(x, lay["attn_norm"])
             qkv = h @ lay["wqkv"].T
