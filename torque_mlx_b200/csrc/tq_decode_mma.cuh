@@ -309,8 +309,11 @@ decode_mma_kernel(DecodeParams p) {
   const int64_t n = unit_length(p, u);
   const int64_t c0 = (int64_t)split * p.chunk;
   const int64_t c1 = min(c0 + (int64_t)p.chunk, n);
-  const int64_t per_warp = p.chunk / kMmaWarps;  // multiple of 16
-  const int64_t w0 = c0 + warp * per_warp;
+  // the CTA's real token range is shared evenly (in 16-token tiles) by its
+  // warps, so a short last split of a ragged sequence still uses every warp
+  const int64_t tiles = c1 > c0 ? (c1 - c0 + 15) / 16 : 0;
+  const int64_t per_warp = (tiles + kMmaWarps - 1) / kMmaWarps * 16;
+  const int64_t w0 = min(c0 + warp * per_warp, max(c1, c0));
   const int64_t w1 = min(w0 + per_warp, c1);
   const uint32_t* kbase = p.k_slab + u * p.unit_stride;
   const uint32_t* vbase = p.v_slab + u * p.unit_stride;
