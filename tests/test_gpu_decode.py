@@ -312,3 +312,19 @@ def test_captured_step_matches_eager_steps(mode):
         np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), atol=1e-6, rtol=1e-6)
     assert list(graph.lengths) == list(eager.lengths) == [503, 80]
     np.testing.assert_array_equal(graph.packed_words()[0], eager.packed_words()[0])
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("b", [2, 3, 4])
+def test_many_units_wide_ctas(d, b):
+    """Batched decode with >= 2 units per SM takes the 16-warp CTA path."""
+    rng = np.random.default_rng(d + b)
+    B, H, G = 40, 8, 4  # 320 units
+    cfg = T.TorqueConfig(bit_width=b, head_dim=d, kv_heads=H)
+    cache = T.TorqueKVCache(config=cfg, batch_size=B, decode_mode="tensor", initial_capacity=256)
+    lens = rng.integers(1, 300, size=B)
+    for s, n in enumerate(lens):
+        cache.append_sequence(s, key=rng.standard_normal((1, H, n, d)).astype(np.float16),
+                              value=rng.standard_normal((1, H, n, d)).astype(np.float16))
+    q = rng.standard_normal((B, 1, H * G, d)).astype(np.float32)
+    np.testing.assert_allclose(cache.decode(query=q), _oracle_for(cache, q), **TOL["tensor"])

@@ -295,6 +295,7 @@ lse_merge_kernel(const float* __restrict__ outs, const float* __restrict__ lses,
 // ---------------------------------------------------------------------------
 struct Plan {
   int mode;       // resolved: exact or tensor
+  int nw;        // warps per CTA (tensor kernel)
   int chunk;      // tokens per CTA
   int splits;     // CTAs per unit
   int warps;      // partials per CTA
@@ -324,9 +325,12 @@ static Plan make_plan(int64_t units, int G, int D, int bits, int64_t max_len, in
   Plan pl;
   pl.mode = resolve_mode(mode, G);
   pl.warps = pl.mode == TQ_DECODE_TENSOR ? 1 : kExactWarps;  // partials per CTA
-  const int tile = pl.mode == TQ_DECODE_TENSOR ? kMmaTokensPerCta : kExactWarps * 32;
-  const int per_sm = pl.mode == TQ_DECODE_TENSOR ? mma_blocks_per_sm(D, bits, G) : 4;
-  const int64_t wave = (int64_t)sm_count() * per_sm;
+  const int sms = sm_count();
+  // batched decode (at least two units per SM): 16-warp CTAs; few long units: 8-warp CTAs
+  pl.nw = (pl.mode == TQ_DECODE_TENSOR && D <= 128 && units >= 2 * (int64_t)sms) ? kMmaWarpsWide : kMmaWarps;
+  const int tile = pl.mode == TQ_DECODE_TENSOR ? pl.nw * 16 : kExactWarps * 32;
+  const int per_sm = pl.mode == TQ_DECODE_TENSOR ? mma_blocks_per_sm(D, bits, G, pl.nw) : 4;
+  const int64_t wave = (int64_t)sms * per_sm;
   const int64_t len = max_len < 1 ? 1 : max_len;
   const int64_t uu = units < 1 ? 1 : units;
   int64_t splits = uu < wave ? (wave + uu - 1) / uu : (4 * wave + uu - 1) / uu;
@@ -433,6 +437,7 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
   p.cent_v = cent_v;
   p.scale_log2 = scale * kLog2e;
   p.chunk = pl.chunk;
+  p.nw = pl.nw;
   p.splits = pl.splits;
   p.part = (float*)workspace;
 

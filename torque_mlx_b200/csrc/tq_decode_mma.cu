@@ -3,45 +3,57 @@
 
 namespace tq {
 
-template <int D, int BITS, int NT>
+template <int D, int BITS, int NT, int NW>
 static void* prepare() {
   // the dynamic shared-memory opt-in, once per process (it is per-function state)
   static const bool done = [] {
-    cudaFuncSetAttribute(decode_mma_kernel<D, BITS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)MmaCfg<D, BITS, NT>::SMEM_BYTES);
+    cudaFuncSetAttribute(decode_mma_kernel<D, BITS, NT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)MmaCfg<D, BITS, NT, NW>::SMEM_BYTES);
     return true;
   }();
   (void)done;
-  return (void*)decode_mma_kernel<D, BITS, NT>;
+  return (void*)decode_mma_kernel<D, BITS, NT, NW>;
 }
 
-template <int D, int BITS, int NT>
+template <int D, int BITS, int NT, int NW>
 static int occupancy() {
+  static int cached = 0;
+  if (cached) return cached;
   int blocks = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, prepare<D, BITS, NT>(), kMmaWarps * 32,
-                                                    MmaCfg<D, BITS, NT>::SMEM_BYTES) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, prepare<D, BITS, NT, NW>(), NW * 32,
+                                                    MmaCfg<D, BITS, NT, NW>::SMEM_BYTES) != cudaSuccess ||
       blocks < 1) {
     cudaGetLastError();
-    blocks = mma_min_blocks<D>();
+    return mma_min_blocks<D, NW>();
   }
+  cached = blocks;
   return blocks;
+}
+
+template <int D, int BITS, int NT, int NW>
+static void launch_one(const DecodeParams& p, cudaStream_t st) {
+  dim3 grid(p.splits, (unsigned)p.units);
+  prepare<D, BITS, NT, NW>();
+  decode_mma_kernel<D, BITS, NT, NW><<<grid, NW * 32, MmaCfg<D, BITS, NT, NW>::SMEM_BYTES, st>>>(p);
 }
 
 template <int D, int BITS>
 static void launch_mma(const DecodeParams& p, cudaStream_t st) {
-  dim3 grid(p.splits, (unsigned)p.units);
+  const bool wide = D <= 128 && p.nw == kMmaWarpsWide;
   if (p.G <= 8) {
-    prepare<D, BITS, 1>();
-    decode_mma_kernel<D, BITS, 1><<<grid, kMmaWarps * 32, MmaCfg<D, BITS, 1>::SMEM_BYTES, st>>>(p);
+    if (wide) launch_one<D, BITS, 1, kMmaWarpsWide>(p, st);
+    else launch_one<D, BITS, 1, kMmaWarps>(p, st);
   } else {
-    prepare<D, BITS, 2>();
-    decode_mma_kernel<D, BITS, 2><<<grid, kMmaWarps * 32, MmaCfg<D, BITS, 2>::SMEM_BYTES, st>>>(p);
+    if (wide) launch_one<D, BITS, 2, kMmaWarpsWide>(p, st);
+    else launch_one<D, BITS, 2, kMmaWarps>(p, st);
   }
 }
 
 template <int D, int BITS>
-static int blocks_for(int G) {
-  return G <= 8 ? occupancy<D, BITS, 1>() : occupancy<D, BITS, 2>();
+static int blocks_for(int G, int nw) {
+  const bool wide = D <= 128 && nw == kMmaWarpsWide;
+  if (G <= 8) return wide ? occupancy<D, BITS, 1, kMmaWarpsWide>() : occupancy<D, BITS, 1, kMmaWarps>();
+  return wide ? occupancy<D, BITS, 2, kMmaWarpsWide>() : occupancy<D, BITS, 2, kMmaWarps>();
 }
 
 #define TQ_DISPATCH(D_, bits_, CALL)                                   \
@@ -61,9 +73,9 @@ void launch_mma_dispatch(int D, int bits, const DecodeParams& p, cudaStream_t st
 #undef CALL_LAUNCH
 }
 
-int mma_blocks_per_sm(int D, int bits, int G) {
+int mma_blocks_per_sm(int D, int bits, int G, int nw) {
   int r = 1;
-#define CALL_OCC(d, b) r = blocks_for<d, b>(G)
+#define CALL_OCC(d, b) r = blocks_for<d, b>(G, nw)
   TQ_DISPATCH(D, bits, CALL_OCC);
 #undef CALL_OCC
   return r;

@@ -54,6 +54,7 @@ struct DecodeParams {
   const float* cent_v;
   float scale_log2;      // softmax scale * log2(e)
   int chunk;             // tokens per CTA
+  int nw;                // warps per CTA of the tensor-core kernel (kMmaWarps or kMmaWarpsWide)
   int splits;            // CTAs per unit
   float* part;           // [units*G, splits*(partials per CTA), D+2]
 };
@@ -65,8 +66,10 @@ __device__ __forceinline__ int64_t unit_length(const DecodeParams& p, int64_t u)
   return n < 0 ? 0 : n;
 }
 
-constexpr int kMmaWarps = 8;                      // warps per CTA
-constexpr int kMmaTokensPerCta = kMmaWarps * 16;  // chunk granule: one tile per warp
+// Warps per CTA: 8 (two CTAs per SM) for few, long units; 16 (one CTA per SM,
+// the tables built once for 16 warps) for batched decode with many units.
+constexpr int kMmaWarps = 8;
+constexpr int kMmaWarpsWide = 16;
 constexpr float kLazyMaxSlack = 8.f;              // log2 headroom before the max is raised
 
 // ---------------------------------------------------------------------------
@@ -212,7 +215,7 @@ __device__ __forceinline__ void pair_tokens(const uint32_t* A, const uint32_t* B
 // ---------------------------------------------------------------------------
 // configuration
 // ---------------------------------------------------------------------------
-template <int D, int BITS, int NT>
+template <int D, int BITS, int NT, int NW = kMmaWarps>
 struct MmaCfg {
   static constexpr int W = D * BITS / 32;     // words per token
   static constexpr int NP = 1 << (2 * BITS);  // pair-table entries
@@ -226,7 +229,7 @@ struct MmaCfg {
   static constexpr int FRAG = NT * KB * 4 * 32;  // accumulator words of one warp
   static constexpr size_t MAIN_BYTES = (size_t)LUT_WORDS * 4 + (size_t)GM * D * 4;
   static constexpr size_t MERGE_BYTES =
-      ((size_t)kMmaWarps * FRAG + 3 * kMmaWarps * GM + 2 * GM) * 4;
+      ((size_t)NW * FRAG + 3 * NW * GM + 2 * GM) * 4;
   static constexpr size_t SMEM_BYTES = MAIN_BYTES > MERGE_BYTES ? MAIN_BYTES : MERGE_BYTES;
 };
 
@@ -278,20 +281,18 @@ __device__ __forceinline__ void load_tile_clamped(TileRegs<D, BITS>& t, const ui
   load_raw<C::RUNV, W>(t.vd, vt + row(2 * tq + 9) + lp.v_word, lp.v_bit);
 }
 
-// d = 256 tiles need more registers; smaller heads run TQ_MINB CTAs per SM.
-#ifndef TQ_MINB
-#define TQ_MINB 2
-#endif
-template <int D>
-constexpr int mma_min_blocks() { return D == 256 ? 1 : TQ_MINB; }
+// d = 256 tiles need more registers (one 8-warp CTA per SM); smaller heads run
+// two 8-warp CTAs or one 16-warp CTA per SM (128 registers a thread either way).
+template <int D, int NW>
+constexpr int mma_min_blocks() { return (D == 256 || NW == kMmaWarpsWide) ? 1 : 2; }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <int D, int BITS, int NT>
-__global__ void __launch_bounds__(kMmaWarps * 32, mma_min_blocks<D>())
+template <int D, int BITS, int NT, int NW>
+__global__ void __launch_bounds__(NW * 32, mma_min_blocks<D, NW>())
 decode_mma_kernel(DecodeParams p) {
-  using C = MmaCfg<D, BITS, NT>;
+  using C = MmaCfg<D, BITS, NT, NW>;
   constexpr int E = D / 32;
   constexpr int KB = C::KB;
   constexpr int GM = C::GM;
@@ -312,7 +313,7 @@ decode_mma_kernel(DecodeParams p) {
   // the CTA's real token range is shared evenly (in 16-token tiles) by its
   // warps, so a short last split of a ragged sequence still uses every warp
   const int64_t tiles = c1 > c0 ? (c1 - c0 + 15) / 16 : 0;
-  const int64_t per_warp = (tiles + kMmaWarps - 1) / kMmaWarps * 16;
+  const int64_t per_warp = (tiles + NW - 1) / NW * 16;
   const int64_t w0 = min(c0 + warp * per_warp, max(c1, c0));
   const int64_t w1 = min(w0 + per_warp, c1);
   const uint32_t* kbase = p.k_slab + u * p.unit_stride;
@@ -338,7 +339,7 @@ decode_mma_kernel(DecodeParams p) {
   // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
   {
     constexpr int MASK = (1 << BITS) - 1;
-    for (int e = tid; e < C::NP; e += kMmaWarps * 32) {
+    for (int e = tid; e < C::NP; e += NW * 32) {
       const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + (e >> BITS)));
       const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + (e >> BITS)));
       uint4* dk = reinterpret_cast<uint4*>(lut + e * 64);
@@ -351,7 +352,7 @@ decode_mma_kernel(DecodeParams p) {
     }
   }
   // ---- query rows: rotate (exact fp32), fold the scale in base 2 ----
-  for (int g = warp; g < GM; g += kMmaWarps) {
+  for (int g = warp; g < GM; g += NW) {
     float v[E];
     if (g < G) {
       const float* q = p.query + (u * G + g) * D;
@@ -503,10 +504,10 @@ decode_mma_kernel(DecodeParams p) {
     }
   __syncthreads();  // all warps are done with the tables
   float* frag = reinterpret_cast<float*>(smem);       // [NW][FRAG] accumulators in fragment order
-  float* red_m = frag + kMmaWarps * C::FRAG;          // [NW][GM]
-  float* red_l = red_m + kMmaWarps * GM;              // [NW][GM]
-  float* scale = red_l + kMmaWarps * GM;              // [NW][GM]
-  float* fin_m = scale + kMmaWarps * GM;              // [GM]
+  float* red_m = frag + NW * C::FRAG;          // [NW][GM]
+  float* red_l = red_m + NW * GM;              // [NW][GM]
+  float* scale = red_l + NW * GM;              // [NW][GM]
+  float* fin_m = scale + NW * GM;              // [GM]
   float* fin_l = fin_m + GM;                          // [GM]
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
@@ -527,9 +528,9 @@ decode_mma_kernel(DecodeParams p) {
   __syncthreads();
   if (tid < GM) {
     float M = -INFINITY;
-    for (int w = 0; w < kMmaWarps; ++w) M = fmaxf(M, red_m[w * GM + tid]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w * GM + tid]);
     float L = 0.f;
-    for (int w = 0; w < kMmaWarps; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float mw = red_m[w * GM + tid];
       const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
       scale[w * GM + tid] = f;
@@ -540,7 +541,7 @@ decode_mma_kernel(DecodeParams p) {
   }
   __syncthreads();
   // element i of a warp's fragment slab = (nt, mb, e, lane) -> (head, dim)
-  for (int i = tid; i < C::FRAG; i += kMmaWarps * 32) {
+  for (int i = tid; i < C::FRAG; i += NW * 32) {
     const int ln = i & 31, e = (i >> 5) & 3, blk = i >> 7;
     const int nt = blk / KB, mb = blk % KB;
     const int g = nt * 8 + 2 * (ln & 3) + (e & 1);
@@ -548,7 +549,7 @@ decode_mma_kernel(DecodeParams p) {
     const int dim = (ln >> 2) * (D / 8) + 2 * mb + (e >> 1);
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kMmaWarps; ++w) acc = fmaf(frag[w * C::FRAG + i], scale[w * GM + g], acc);
+    for (int w = 0; w < NW; ++w) acc = fmaf(frag[w * C::FRAG + i], scale[w * GM + g], acc);
     p.part[((u * G + g) * (int64_t)p.splits + split) * (D + 2) + dim] = acc;
   }
   if (tid < G && tid < GM) {
@@ -560,7 +561,7 @@ decode_mma_kernel(DecodeParams p) {
 
 // Launches the tensor-core kernel for (D, BITS) (tq_decode_mma.cu).
 void launch_mma_dispatch(int D, int bits, const DecodeParams& p, cudaStream_t st);
-// Resident CTAs per SM of the tensor-core kernel for (D, BITS, G).
-int mma_blocks_per_sm(int D, int bits, int G);
+// Resident CTAs per SM of the tensor-core kernel for (D, BITS, G, warps per CTA).
+int mma_blocks_per_sm(int D, int bits, int G, int nw);
 
 }  // namespace tq
