@@ -25,8 +25,8 @@
 //    reference max: probabilities are exp2(s - m) with m shared by the lanes of
 //    a head; m is only raised (shuffle max + rescale) when a score exceeds it
 //    by more than 8, so p <= 256 stays exact in fp16 and most tiles need no
-//    cross-lane reduction.  P is rounded to fp16 once and the same values feed
-//    P.V and the denominator.  The C->B fragment transpose of P is movmatrix.
+//    cross-lane reduction.  P.V uses P rounded to fp16, the denominator sums
+//    the fp32 values.  The C->B fragment transpose of P is movmatrix.
 //  * the warps' accumulators are merged through shared memory (fragment
 //    slabs, read back conflict-free); one partial (o, m, l) per query row and
 //    split goes to the split-merge kernel.
@@ -387,10 +387,11 @@ decode_mma_kernel(DecodeParams p) {
     for (int kb = 0; kb < KB; ++kb)
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[nt][kb][e] = 0.f;
-  float mref[NT][2], lrow[NT][2];  // reference max (uniform over the 8 lanes of a head), row sums
+  float mref[NT][2], mthr[NT][2], lrow[NT][2];  // reference max (uniform over a head's 8 lanes), + slack, row sums
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     mref[nt][0] = mref[nt][1] = -INFINITY;
+    mthr[nt][0] = mthr[nt][1] = -INFINITY;
     lrow[nt][0] = lrow[nt][1] = 0.f;
   }
   const uint32_t lane4 = (uint32_t)lane * 4u;
@@ -418,17 +419,23 @@ decode_mma_kernel(DecodeParams p) {
       }
     }
     // ---------------- online softmax with a lazy reference max ----------------
-    const bool v0 = gr < valid, v1 = gr + 8 < valid;
     bool raise = false;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        sc[nt][e] += sd[nt][e];
-        const bool v = (e < 2) ? v0 : v1;
-        if (!v) sc[nt][e] = -INFINITY;
-        raise |= sc[nt][e] > mref[nt][e & 1] + kLazyMaxSlack;
-      }
+      for (int e = 0; e < 4; ++e) sc[nt][e] += sd[nt][e];
+    if (valid < 16) {  // only the last tile of a range is partial
+      const bool v0 = gr < valid, v1 = gr + 8 < valid;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (!((e < 2) ? v0 : v1)) sc[nt][e] = -INFINITY;
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) raise |= sc[nt][e] > mthr[nt][e & 1];
     if (__any_sync(FULL, raise)) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -441,6 +448,7 @@ decode_mma_kernel(DecodeParams p) {
           const float mn = fmaxf(mref[nt][e], tm);
           const float alpha = fast_exp2(mref[nt][e] - mn);  // -inf -> 0
           mref[nt][e] = mn;
+          mthr[nt][e] = mn + kLazyMaxSlack;
           lrow[nt][e] *= alpha;
 #pragma unroll
           for (int kb = 0; kb < KB; ++kb) {
@@ -452,11 +460,12 @@ decode_mma_kernel(DecodeParams p) {
     uint32_t pb[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const __half2 lo = __floats2half2_rn(fast_exp2(sc[nt][0] - mref[nt][0]), fast_exp2(sc[nt][1] - mref[nt][1]));
-      const __half2 hi = __floats2half2_rn(fast_exp2(sc[nt][2] - mref[nt][0]), fast_exp2(sc[nt][3] - mref[nt][1]));
-      const float2 lf = __half22float2(lo), hf = __half22float2(hi);
-      lrow[nt][0] += lf.x + hf.x;
-      lrow[nt][1] += lf.y + hf.y;
+      const float p0 = fast_exp2(sc[nt][0] - mref[nt][0]), p1 = fast_exp2(sc[nt][1] - mref[nt][1]);
+      const float p2 = fast_exp2(sc[nt][2] - mref[nt][0]), p3 = fast_exp2(sc[nt][3] - mref[nt][1]);
+      const __half2 lo = __floats2half2_rn(p0, p1);
+      const __half2 hi = __floats2half2_rn(p2, p3);
+      lrow[nt][0] += p0 + p2;
+      lrow[nt][1] += p1 + p3;
       pb[nt][0] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&lo));  // tokens 2c, 2c+1 of head r
       pb[nt][1] = movmatrix_trans(*reinterpret_cast<const uint32_t*>(&hi));  // tokens 2c+8, 2c+9
     }
