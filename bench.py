@@ -39,6 +39,10 @@ WORKLOADS = {
                     seed=4, steps=2000,
                     desc="BASELINE config 4: batched decode, batch 64/GPU x 16K-32K tokens, 32q/8kv heads, d128, "
                          "3-bit"),
+    "config4_4bit": dict(batch=64, q_heads=32, kv_heads=8, head_dim=128, bits=4, len_lo=16384, len_hi=32768,
+                         seed=4, steps=2000,
+                         desc="config-4 geometry at 4 bits (the north-star bit width): batch 64/GPU x 16K-32K "
+                              "tokens, 32q/8kv heads, d128"),
     "config3": dict(batch=1, q_heads=16, kv_heads=2, head_dim=256, bits=4, len_lo=131072, len_hi=131072, seed=3,
                     steps=5000,
                     desc="BASELINE config 3: long-context batch-1 decode, 131072 tokens, 16q/2kv heads, d256, 4-bit"),

@@ -104,27 +104,30 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
 
 // Pair tables: K and V entries interleave with a 256-byte stride per entry,
 // K entry e of lane l at byte e*256 + 4l and V entry e at byte e*256 + 128 + 4l,
-// so one offset serves both tables and every lane reads its own bank.
+// so one offset serves both tables and every lane reads its own bank.  Entries
+// are indexed by a whole byte: the low 2b bits are the code pair, any higher
+// bits are ignored (the entry is repeated for them).
 //
-// Byte offset e*256 + 4*lane of the NB-bit field e at static bit `bit` of the
-// run registers r[].  Byte-aligned 8-bit fields (4-bit codes) take a single
-// byte permute that also inserts the lane term; other fields shift the field
-// to bit 8 and mask, with the lane term ORed in by the same logic op.
-template <int NB>
-__device__ __forceinline__ uint32_t lut_off(const uint32_t* r, int bit, uint32_t lane4) {
-  const int w = bit >> 5, s = bit & 31;
-  if constexpr (NB == 8) {
-    if ((s & 7) == 0) {
-      // result bytes: [lane4, field byte, 0, 0]; selector nibbles index bytes of {r[w], lane4}
-      return __byte_perm(r[w], lane4, 0x5504u | ((uint32_t)(s >> 3) << 4));
-    }
+// A pair field of 2b bits starts at an even bit of the run.  Copies of the
+// run shifted right by 0, 2, 4 and 6 bits (funnel shifts, built once per run)
+// put every field at the start of a byte of one copy, so a single byte
+// permute yields the byte offset e*256 + 4*lane for any field.
+template <int N>
+__device__ __forceinline__ void shifted_copies(const uint32_t (&r)[N], uint32_t (&c)[4][N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    c[0][i] = r[i];
+#pragma unroll
+    for (int k = 1; k < 4; ++k) c[k][i] = i + 1 < N ? __funnelshift_r(r[i], r[i + 1], 2 * k) : (r[i] >> (2 * k));
   }
-  constexpr uint32_t M = ((1u << NB) - 1u) << 8;
-  uint32_t v;
-  if (s + NB > 32) v = __funnelshift_r(r[w], r[w + 1], s) << 8;
-  else if (s >= 8) v = r[w] >> (s - 8);
-  else v = r[w] << (8 - s);
-  return (v & M) | lane4;
+}
+
+template <int N>
+__device__ __forceinline__ uint32_t lut_off(const uint32_t (&c)[4][N], int bit, uint32_t lane4) {
+  const int k = bit & 7;          // even for every pair field
+  const int aligned = bit - k;    // byte-aligned start in copy k/2
+  // result bytes: [lane4, field byte, 0, 0]; selector nibbles index bytes of {word, lane4}
+  return __byte_perm(c[k >> 1][aligned >> 5], lane4, 0x5504u | ((uint32_t)((aligned >> 3) & 3) << 4));
 }
 
 constexpr uint32_t kLutVOffset = 128;  // V entry follows the K entry inside a 256-byte row
@@ -218,7 +221,7 @@ __device__ __forceinline__ void pair_tokens(const uint32_t* A, const uint32_t* B
 template <int D, int BITS, int NT, int NW = kMmaWarps>
 struct MmaCfg {
   static constexpr int W = D * BITS / 32;     // words per token
-  static constexpr int NP = 1 << (2 * BITS);  // pair-table entries
+  static constexpr int NP = 256;              // pair-table entries (indexed by a byte)
   static constexpr int LUT_WORDS = NP * 64;   // K + V tables, 256 B per entry (one copy per lane each)
   static constexpr int RUNK = D / 4 * BITS;   // K bits per lane
   static constexpr int RUNV = D / 8 * BITS;   // V bits per lane
@@ -340,8 +343,8 @@ decode_mma_kernel(DecodeParams p) {
   {
     constexpr int MASK = (1 << BITS) - 1;
     for (int e = tid; e < C::NP; e += NW * 32) {
-      const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + (e >> BITS)));
-      const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + (e >> BITS)));
+      const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + ((e >> BITS) & MASK)));
+      const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + ((e >> BITS) & MASK)));
       uint4* dk = reinterpret_cast<uint4*>(lut + e * 64);
       uint4* dv = reinterpret_cast<uint4*>(lut + e * 64 + 32);
 #pragma unroll
@@ -406,12 +409,15 @@ decode_mma_kernel(DecodeParams p) {
     uint32_t k0[C::RK], k1[C::RK];
     align_run<C::RUNK>(k0, t.k0, lp.k_bit);
     align_run<C::RUNK>(k1, t.k1, lp.k_bit);
+    uint32_t kc0[4][C::RK], kc1[4][C::RK];
+    shifted_copies(k0, kc0);
+    shifted_copies(k1, kc1);
 #pragma unroll
     for (int kb = 0; kb < KB; ++kb) {
-      const uint32_t a0 = lut_ld(lut, lut_off<PB>(k0, (2 * kb) * PB, lane4));
-      const uint32_t a1 = lut_ld(lut, lut_off<PB>(k1, (2 * kb) * PB, lane4));
-      const uint32_t a2 = lut_ld(lut, lut_off<PB>(k0, (2 * kb + 1) * PB, lane4));
-      const uint32_t a3 = lut_ld(lut, lut_off<PB>(k1, (2 * kb + 1) * PB, lane4));
+      const uint32_t a0 = lut_ld(lut, lut_off(kc0, (2 * kb) * PB, lane4));
+      const uint32_t a1 = lut_ld(lut, lut_off(kc1, (2 * kb) * PB, lane4));
+      const uint32_t a2 = lut_ld(lut, lut_off(kc0, (2 * kb + 1) * PB, lane4));
+      const uint32_t a3 = lut_ld(lut, lut_off(kc1, (2 * kb + 1) * PB, lane4));
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         if (kb & 1) mma_f16(sd[nt], a0, a1, a2, a3, qf[nt][kb][0], qf[nt][kb][1]);
@@ -481,12 +487,17 @@ decode_mma_kernel(DecodeParams p) {
     pair_tokens<BITS, NR>(vc, vd, ec, oc);
     ea[NR] = oa[NR] = ec[NR] = oc[NR] = 0;
     // m-block mb: run code 2mb (row r) and 2mb+1 (row r+8) = field mb of ev / od
+    uint32_t ca[4][C::RV], cb[4][C::RV], cc[4][C::RV], cd[4][C::RV];
+    shifted_copies(ea, ca);
+    shifted_copies(oa, cb);
+    shifted_copies(ec, cc);
+    shifted_copies(oc, cd);
 #pragma unroll
     for (int mb = 0; mb < KB; ++mb) {
-      const uint32_t a0 = lut_ld(lut, lut_off<PB>(ea, mb * PB, lane4) + kLutVOffset);
-      const uint32_t a1 = lut_ld(lut, lut_off<PB>(oa, mb * PB, lane4) + kLutVOffset);
-      const uint32_t a2 = lut_ld(lut, lut_off<PB>(ec, mb * PB, lane4) + kLutVOffset);
-      const uint32_t a3 = lut_ld(lut, lut_off<PB>(oc, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a0 = lut_ld(lut, lut_off(ca, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a1 = lut_ld(lut, lut_off(cb, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a2 = lut_ld(lut, lut_off(cc, mb * PB, lane4) + kLutVOffset);
+      const uint32_t a3 = lut_ld(lut, lut_off(cd, mb * PB, lane4) + kLutVOffset);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma_f16(o[nt][mb], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
     }
