@@ -284,122 +284,16 @@ __device__ __forceinline__ void load_tile_clamped(TileRegs<D, BITS>& t, const ui
   load_raw<C::RUNV, W>(t.vd, vt + row(2 * tq + 9) + lp.v_word, lp.v_bit);
 }
 
-// d = 256 tiles need more registers (one 8-warp CTA per SM); smaller heads run
-// two 8-warp CTAs or one 16-warp CTA per SM (128 registers a thread either way).
-template <int D, int NW>
-constexpr int mma_min_blocks() { return (D == 256 || NW == kMmaWarpsWide) ? 1 : 2; }
-
-// ---------------------------------------------------------------------------
-// the kernel
-// ---------------------------------------------------------------------------
-template <int D, int BITS, int NT, int NW>
-__global__ void __launch_bounds__(NW * 32, mma_min_blocks<D, NW>())
-decode_mma_kernel(DecodeParams p) {
-  using C = MmaCfg<D, BITS, NT, NW>;
-  constexpr int E = D / 32;
+// One 16-token tile of a warp: scores, online softmax, P.V into the warp's
+// accumulators (o, reference max, threshold, row sums).
+template <int D, int BITS, int NT>
+__device__ __forceinline__ void tile_math(const TileRegs<D, BITS>& t, int valid, const uint32_t* lut,
+                                          const LanePlan& lp, uint32_t lane4, int gr, int tq,
+                                          const uint32_t (&qf)[NT][D / 16][2], float (&o)[NT][D / 16][4],
+                                          float (&mref)[NT][2], float (&mthr)[NT][2], float (&lrow)[NT][2]) {
+  using C = MmaCfg<D, BITS, NT>;
   constexpr int KB = C::KB;
-  constexpr int GM = C::GM;
-  constexpr int PB = 2 * BITS;  // bits of a code pair
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);      // interleaved K/V pair tables
-  float* q_s = reinterpret_cast<float*>(lut + C::LUT_WORDS);  // [GM][D]
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int gr = lane >> 2, tq = lane & 3;
-  const int64_t u = blockIdx.y;
-  const int split = blockIdx.x;
-  const int G = p.G;
-
-  const int64_t n = unit_length(p, u);
-  const int64_t c0 = (int64_t)split * p.chunk;
-  const int64_t c1 = min(c0 + (int64_t)p.chunk, n);
-  // the CTA's real token range is shared evenly (in 16-token tiles) by its
-  // warps, so a short last split of a ragged sequence still uses every warp
-  const int64_t tiles = c1 > c0 ? (c1 - c0 + 15) / 16 : 0;
-  const int64_t per_warp = (tiles + NW - 1) / NW * 16;
-  const int64_t w0 = min(c0 + warp * per_warp, max(c1, c0));
-  const int64_t w1 = min(w0 + per_warp, c1);
-  const uint32_t* kbase = p.k_slab + u * p.unit_stride;
-  const uint32_t* vbase = p.v_slab + u * p.unit_stride;
-
-  // lane load plan and the first tile (in flight while the tables are built)
-  LanePlan lp;
-  lp.k_word = (tq * C::RUNK) >> 5;
-  lp.k_bit = (tq * C::RUNK) & 31;
-  lp.v_word = (gr * C::RUNV) >> 5;
-  lp.v_bit = (gr * C::RUNV) & 31;
-  lp.k_row = gr * C::W + lp.k_word;
-  lp.v_row = 2 * tq * C::W + lp.v_word;
-  auto fetch = [&](TileRegs<D, BITS>& t, int64_t tile0) {
-    const uint32_t* k = kbase + tile0 * C::W;
-    const uint32_t* v = vbase + tile0 * C::W;
-    if (tile0 + 16 <= n) load_tile<D, BITS>(t, k, v, lp);
-    else load_tile_clamped<D, BITS>(t, k, v, (int)(n - 1 - tile0), gr, tq, lp);
-  };
-  TileRegs<D, BITS> ta, tb;
-  if (w0 < w1) fetch(ta, w0);
-
-  // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
-  {
-    constexpr int MASK = (1 << BITS) - 1;
-    for (int e = tid; e < C::NP; e += NW * 32) {
-      const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + ((e >> BITS) & MASK)));
-      const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + ((e >> BITS) & MASK)));
-      uint4* dk = reinterpret_cast<uint4*>(lut + e * 64);
-      uint4* dv = reinterpret_cast<uint4*>(lut + e * 64 + 32);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        dk[i] = make_uint4(hk, hk, hk, hk);
-        dv[i] = make_uint4(hv, hv, hv, hv);
-      }
-    }
-  }
-  // ---- query rows: rotate (exact fp32), fold the scale in base 2 ----
-  for (int g = warp; g < GM; g += NW) {
-    float v[E];
-    if (g < G) {
-      const float* q = p.query + (u * G + g) * D;
-#pragma unroll
-      for (int j = 0; j < E; ++j) v[j] = __ldg(q + j * 32 + lane);
-      if (p.rotate_query) warp_rotate<D>(v, lane, p.signs_right, p.signs_left);
-    } else {
-#pragma unroll
-      for (int j = 0; j < E; ++j) v[j] = 0.f;
-    }
-#pragma unroll
-    for (int j = 0; j < E; ++j) q_s[g * D + j * 32 + lane] = v[j] * p.scale_log2;
-  }
-  __syncthreads();
-
-  // B fragments of the score mma: lane (r, c) holds head r (+8 nt) at dims
-  // c*D/4 + 4kb + {0,1} and {2,3}, the same permutation as the K runs.
-  uint32_t qf[NT][KB][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int kb = 0; kb < KB; ++kb) {
-      const float* qr = q_s + (nt * 8 + gr) * D + tq * (D / 4) + 4 * kb;
-      qf[nt][kb][0] = pack_half2(qr[0], qr[1]);
-      qf[nt][kb][1] = pack_half2(qr[2], qr[3]);
-    }
-
-  float o[NT][KB][4];  // O^T accumulators: m-block kb, n-tile nt
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-    for (int kb = 0; kb < KB; ++kb)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[nt][kb][e] = 0.f;
-  float mref[NT][2], mthr[NT][2], lrow[NT][2];  // reference max (uniform over a head's 8 lanes), + slack, row sums
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    mref[nt][0] = mref[nt][1] = -INFINITY;
-    mthr[nt][0] = mthr[nt][1] = -INFINITY;
-    lrow[nt][0] = lrow[nt][1] = 0.f;
-  }
-  const uint32_t lane4 = (uint32_t)lane * 4u;
-
-  auto process = [&](const TileRegs<D, BITS>& t, int valid) {
+  constexpr int PB = 2 * BITS;
     // ---------------- scores S[t, g] (two independent accumulator chains) ----------------
     float sc[NT][4], sd[NT][4];
 #pragma unroll
@@ -501,6 +395,124 @@ decode_mma_kernel(DecodeParams p) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma_f16(o[nt][mb], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
     }
+}
+
+// d = 256 tiles need more registers (one 8-warp CTA per SM); smaller heads run
+// two 8-warp CTAs or one 16-warp CTA per SM (128 registers a thread either way).
+template <int D, int NW>
+constexpr int mma_min_blocks() { return (D == 256 || NW == kMmaWarpsWide) ? 1 : 2; }
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int D, int BITS, int NT, int NW>
+__global__ void __launch_bounds__(NW * 32, mma_min_blocks<D, NW>())
+decode_mma_kernel(DecodeParams p) {
+  using C = MmaCfg<D, BITS, NT, NW>;
+  constexpr int E = D / 32;
+  constexpr int KB = C::KB;
+  constexpr int GM = C::GM;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t* lut = reinterpret_cast<uint32_t*>(smem);      // interleaved K/V pair tables
+  float* q_s = reinterpret_cast<float*>(lut + C::LUT_WORDS);  // [GM][D]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int gr = lane >> 2, tq = lane & 3;
+  const int64_t u = blockIdx.y;
+  const int split = blockIdx.x;
+  const int G = p.G;
+
+  const int64_t n = unit_length(p, u);
+  const int64_t c0 = (int64_t)split * p.chunk;
+  const int64_t c1 = min(c0 + (int64_t)p.chunk, n);
+  // the CTA's real token range is shared evenly (in 16-token tiles) by its
+  // warps, so a short last split of a ragged sequence still uses every warp
+  const int64_t tiles = c1 > c0 ? (c1 - c0 + 15) / 16 : 0;
+  const int64_t per_warp = (tiles + NW - 1) / NW * 16;
+  const int64_t w0 = min(c0 + warp * per_warp, max(c1, c0));
+  const int64_t w1 = min(w0 + per_warp, c1);
+  const uint32_t* kbase = p.k_slab + u * p.unit_stride;
+  const uint32_t* vbase = p.v_slab + u * p.unit_stride;
+
+  // lane load plan and the first tile (in flight while the tables are built)
+  LanePlan lp;
+  lp.k_word = (tq * C::RUNK) >> 5;
+  lp.k_bit = (tq * C::RUNK) & 31;
+  lp.v_word = (gr * C::RUNV) >> 5;
+  lp.v_bit = (gr * C::RUNV) & 31;
+  lp.k_row = gr * C::W + lp.k_word;
+  lp.v_row = 2 * tq * C::W + lp.v_word;
+  auto fetch = [&](TileRegs<D, BITS>& t, int64_t tile0) {
+    const uint32_t* k = kbase + tile0 * C::W;
+    const uint32_t* v = vbase + tile0 * C::W;
+    if (tile0 + 16 <= n) load_tile<D, BITS>(t, k, v, lp);
+    else load_tile_clamped<D, BITS>(t, k, v, (int)(n - 1 - tile0), gr, tq, lp);
+  };
+  TileRegs<D, BITS> ta, tb;
+  if (w0 < w1) fetch(ta, w0);
+
+  // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
+  {
+    constexpr int MASK = (1 << BITS) - 1;
+    for (int e = tid; e < C::NP; e += NW * 32) {
+      const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + ((e >> BITS) & MASK)));
+      const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + ((e >> BITS) & MASK)));
+      uint4* dk = reinterpret_cast<uint4*>(lut + e * 64);
+      uint4* dv = reinterpret_cast<uint4*>(lut + e * 64 + 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dk[i] = make_uint4(hk, hk, hk, hk);
+        dv[i] = make_uint4(hv, hv, hv, hv);
+      }
+    }
+  }
+  // ---- query rows: rotate (exact fp32), fold the scale in base 2 ----
+  for (int g = warp; g < GM; g += NW) {
+    float v[E];
+    if (g < G) {
+      const float* q = p.query + (u * G + g) * D;
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = __ldg(q + j * 32 + lane);
+      if (p.rotate_query) warp_rotate<D>(v, lane, p.signs_right, p.signs_left);
+    } else {
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < E; ++j) q_s[g * D + j * 32 + lane] = v[j] * p.scale_log2;
+  }
+  __syncthreads();
+
+  // B fragments of the score mma: lane (r, c) holds head r (+8 nt) at dims
+  // c*D/4 + 4kb + {0,1} and {2,3}, the same permutation as the K runs.
+  uint32_t qf[NT][KB][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int kb = 0; kb < KB; ++kb) {
+      const float* qr = q_s + (nt * 8 + gr) * D + tq * (D / 4) + 4 * kb;
+      qf[nt][kb][0] = pack_half2(qr[0], qr[1]);
+      qf[nt][kb][1] = pack_half2(qr[2], qr[3]);
+    }
+
+  float o[NT][KB][4];  // O^T accumulators: m-block kb, n-tile nt
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[nt][kb][e] = 0.f;
+  float mref[NT][2], mthr[NT][2], lrow[NT][2];  // reference max (uniform over a head's 8 lanes), + slack, row sums
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    mref[nt][0] = mref[nt][1] = -INFINITY;
+    mthr[nt][0] = mthr[nt][1] = -INFINITY;
+    lrow[nt][0] = lrow[nt][1] = 0.f;
+  }
+  const uint32_t lane4 = (uint32_t)lane * 4u;
+
+  auto process = [&](const TileRegs<D, BITS>& t, int valid) {
+    tile_math<D, BITS, NT>(t, valid, lut, lp, lane4, gr, tq, qf, o, mref, mthr, lrow);
   };
   // ping-pong: the next tile's loads are issued before the current tile's math
   for (int64_t t0 = w0; t0 < w1; t0 += 32) {
