@@ -46,7 +46,19 @@ def _worker(rank, world, port, q):
         full = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H))
         full.append(key=keys, value=vals)
         ref = full.decode(query=qry)
-        q.put((rank, float(np.max(np.abs(got - ref)))))
+        err = float(np.max(np.abs(got - ref)))
+        # graph-captured steps with new tokens on the last rank
+        plan2 = SequencePlan(world=world, prefill=n, append_to_last=True)
+        dec2 = SequenceShardedDecoder(T.TorqueKVCache(config=cfg), plan2)
+        dec2.prefill(keys[:, a:b], vals[:, a:b])
+        kt = torch.from_numpy(keys[:, n]).cuda()
+        vt = torch.from_numpy(vals[:, n]).cuda()
+        dec2.capture_step(kt, vt, torch.from_numpy(qry).cuda())
+        got2 = dec2.step_graph().cpu().numpy()
+        full2 = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H))
+        full2.append(key=keys[:, :n + 1], value=vals[:, :n + 1])
+        err = max(err, float(np.max(np.abs(got2 - full2.decode(query=qry)))))
+        q.put((rank, err))
     finally:
         dist.destroy_process_group()
 

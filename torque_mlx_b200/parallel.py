@@ -36,10 +36,14 @@ def shard_batch(batch: int, rank: int, world: int) -> tuple[int, int]:
 
 @dataclass
 class SequencePlan:
-    """Which rank holds which token positions of one sequence."""
+    """Which rank holds which token positions of one sequence: contiguous
+    prefill shards, then new tokens round robin (``append_to_last=False``) or
+    all on the last rank (``True``, which keeps every rank's decode step the
+    same each time, so it can be captured in a CUDA graph)."""
 
     world: int
     prefill: int
+    append_to_last: bool = False
 
     def prefill_range(self, rank: int) -> tuple[int, int]:
         """Contiguous share of the prefill tokens."""
@@ -51,6 +55,8 @@ class SequencePlan:
             base, extra = divmod(self.prefill, self.world)
             big = extra * (base + 1)
             return position // (base + 1) if position < big else extra + (position - big) // max(base, 1)
+        if self.append_to_last:
+            return self.world - 1
         return (position - self.prefill) % self.world
 
     def local_count(self, rank: int, length: int) -> int:
@@ -58,6 +64,8 @@ class SequencePlan:
         a, b = self.prefill_range(rank)
         n = b - a
         extra = max(0, length - self.prefill)
+        if self.append_to_last:
+            return n + (extra if rank == self.world - 1 else 0)
         n += extra // self.world + (1 if rank < extra % self.world else 0)
         return n
 
@@ -110,6 +118,50 @@ class SequenceShardedDecoder:
             self.cache.append(key=key, value=value)
         self.length += 1
 
+    def capture_step(self, key, value, query) -> None:
+        """Capture append (on the owning rank) + local decode + all-gather +
+        merge as one CUDA graph; needs ``plan.append_to_last``.  Replay with
+        ``step_graph``; inputs are copied from the given example tensors."""
+        if not self.plan.append_to_last:
+            raise ValueError("graph capture needs SequencePlan(append_to_last=True)")
+        from . import ops
+        c = self.cache
+        self.owner = self.rank == self.world - 1
+        self._k = c._norm_kv(key, "key").clone()
+        self._v = c._norm_kv(value, "value").to(self._k.dtype).clone()
+        q, hq, self._qshape = c._norm_query(query)
+        self._q = q.clone()
+        c._ensure_capacity(c.sequence_length + 1)
+        d = c.config.head_dim
+        rows = self._q.shape[0]
+        # warm the collective and the workspace outside capture
+        out, lse = c._decode(self._q, hq, extra=0, return_lse=True, full_capacity=True)
+        gather_partials(out, lse, self.group)
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=side):
+                if self.owner:
+                    c._write(self._k, self._v)
+                    c._advance_device(1)
+                o, s = c._decode(self._q, hq, extra=0, return_lse=True, full_capacity=True)
+                outs, lses = gather_partials(o, s, self.group)
+                self._out = ops.lse_merge(outs, lses, inverse_rotation=c.rotation if self.rotate_back else None)
+        torch.cuda.current_stream().wait_stream(side)
+        assert self._out.shape == (rows, d)
+
+    def step_graph(self):
+        """Replay the captured step (append the captured token, decode)."""
+        if self.owner and self.cache.capacity - self.cache.sequence_length < 1:
+            raise RuntimeError("cache capacity reached: capture again")
+        self.graph.replay()
+        if self.owner:
+            self.cache._len_host += 1
+        self.length += 1
+        return self._out.reshape(self._qshape)
+
     def decode(self, query):
         """Full-sequence decode: local partial -> all-gather -> LSE merge."""
         from . import ops
@@ -133,10 +185,11 @@ def run_sequence_split_bench(args, wl, rank: int, world: int) -> None:
     dev = torch.device("cuda", torch.cuda.current_device())
     H, Hq, d, bits = wl["kv_heads"], wl["q_heads"], wl["head_dim"], wl["bits"]
     L = wl["len_lo"]
-    plan = SequencePlan(world=world, prefill=L)
+    plan = SequencePlan(world=world, prefill=L, append_to_last=True)
     a, b = plan.prefill_range(rank)
     cfg = T.TorqueConfig(bit_width=bits, head_dim=d, num_layers=1, kv_heads=H, rotation_seed=0, fused_weights=True)
-    cache = T.TorqueKVCache(config=cfg, initial_capacity=(b - a) + args.warmup + args.steps + 512)
+    cache = T.TorqueKVCache(config=cfg, initial_capacity=(b - a) + (args.warmup + args.steps + 512
+                                                                    if rank == world - 1 else 128))
     gen = torch.Generator(device=dev)
     gen.manual_seed(wl["seed"] * 7919 + rank)
     for s in range(a, b, 16384):
@@ -150,18 +203,16 @@ def run_sequence_split_bench(args, wl, rank: int, world: int) -> None:
     new_k = torch.randn((ring, 1, H, d), generator=gen, device=dev, dtype=torch.float16)
     new_v = torch.randn((ring, 1, H, d), generator=gen, device=dev, dtype=torch.float16)
     qs = torch.randn((ring, 1, Hq, d), generator=gen, device=dev, dtype=torch.float32)
-    for i in range(args.warmup):
-        dec.append(new_k[i % ring], new_v[i % ring])
-        dec.decode(qs[i % ring])
+    dec.capture_step(new_k[0], new_v[0], qs[0])  # one CUDA graph per rank: append, decode, all-gather, merge
+    for _ in range(args.warmup):
+        dec.step_graph()
     torch.cuda.synchronize()
     dist.barrier()
     stream = torch.cuda.current_stream()
     s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s0.record(stream)
-    for j in range(args.steps):
-        r = (args.warmup + j) % ring
-        dec.append(new_k[r], new_v[r])
-        dec.decode(qs[r])
+    for _ in range(args.steps):
+        dec.step_graph()
     s1.record(stream)
     torch.cuda.synchronize()
     t = torch.tensor([s0.elapsed_time(s1)], device=dev)
@@ -181,7 +232,8 @@ def run_sequence_split_bench(args, wl, rank: int, world: int) -> None:
             "scaling": "strong", "vs_baseline": None, "dtype": f"u32 packed {bits}-bit codes; fp16 mma",
             "data": "synthetic (seeded fp16 N(0,1) K/V)",
             "config": {"workload": args.workload, "desc": wl["desc"], "global_batch": 1,
-                       "parallelism": f"sequence-split x{world} + NCCL all-gather + LSE merge"},
+                       "parallelism": f"sequence-split x{world} + NCCL all-gather + LSE merge",
+                       "timing": "one CUDA graph per rank per step (append on the last rank, decode, all-gather, merge)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_kind": kind,
                          "note": "per-GPU packed bytes / whole step time (decode + all-gather + merge)"},
