@@ -279,7 +279,9 @@ def run_ours(args, wl) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        from datetime import timedelta
+        # a stuck peer ends the run with an error instead of the 10-minute default wait
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=180))
     if wl["batch"] == 1 and world > 1:
         from torque_mlx_b200.parallel import run_sequence_split_bench
         run_sequence_split_bench(args, wl, rank, world)

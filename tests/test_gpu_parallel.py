@@ -6,6 +6,7 @@ from __future__ import annotations
 
 import os
 import socket
+from datetime import timedelta
 
 import numpy as np
 import pytest
@@ -28,7 +29,8 @@ def _worker(rank, world, port, q):
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=timedelta(seconds=60))
     try:
         rng = np.random.default_rng(5)
         H, G, d, n, extra = 2, 8, 256, 3000, 5
@@ -58,6 +60,8 @@ def _worker(rank, world, port, q):
         full2 = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H))
         full2.append(key=keys[:, :n + 1], value=vals[:, :n + 1])
         err = max(err, float(np.max(np.abs(got2 - full2.decode(query=qry)))))
+        dec2.release()
+        torch.cuda.synchronize()
         q.put((rank, err))
     finally:
         dist.destroy_process_group()
@@ -73,8 +77,14 @@ def test_sequence_sharded_decode_matches_single_rank():
     procs = [ctx.Process(target=_worker, args=(r, world, port, qu)) for r in range(world)]
     for p in procs:
         p.start()
-    for p in procs:
-        p.join(timeout=300)
-        assert p.exitcode == 0
+    try:
+        for p in procs:
+            p.join(timeout=180)
+            assert p.exitcode == 0
+    finally:
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=10)
     errs = dict(qu.get(timeout=5) for _ in range(world))
     assert max(errs.values()) < 2e-4, errs

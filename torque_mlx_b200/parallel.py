@@ -8,7 +8,7 @@ The reference runs on one device only; these partitions are new.
 
 * Sequence sharding (long batch-1 contexts): each rank
   owns a contiguous share of the prefill tokens plus the new tokens it is
-  assigned round-robin.  A decode step is
+  assigned (round robin, or all on the last rank for graph-captured steps).  A decode step is
       local tq_decode over the rank's tokens -> (o_r rotated, lse_r)
       all-gather of [o_r | lse_r] over the process group (NCCL over NVLink)
       tq_lse_merge:  o = sum_r exp(lse_r - LSE) o_r  (then Pi^T)
@@ -119,9 +119,14 @@ class SequenceShardedDecoder:
         self.length += 1
 
     def capture_step(self, key, value, query) -> None:
-        """Capture append (on the owning rank) + local decode + all-gather +
-        merge as one CUDA graph; needs ``plan.append_to_last``.  Replay with
-        ``step_graph``; inputs are copied from the given example tensors."""
+        """Capture one decode step for replay; needs ``plan.append_to_last``.
+
+        Two CUDA graphs around one eager collective: ``local`` (append on the
+        owning rank, local decode, partials staged into the static
+        ``[rows, d + 1]`` send buffer), the NCCL all-gather issued eagerly on
+        the same stream, and ``merge`` (tq_lse_merge + inverse rotation).  The
+        collective stays outside the graphs so no graph holds communicator
+        resources.  Inputs are copied from the example tensors."""
         if not self.plan.append_to_last:
             raise ValueError("graph capture needs SequencePlan(append_to_last=True)")
         from . import ops
@@ -134,33 +139,59 @@ class SequenceShardedDecoder:
         c._ensure_capacity(c.sequence_length + 1)
         d = c.config.head_dim
         rows = self._q.shape[0]
-        # warm the collective and the workspace outside capture
-        out, lse = c._decode(self._q, hq, extra=0, return_lse=True, full_capacity=True)
-        gather_partials(out, lse, self.group)
+        self._send = torch.empty((rows, d + 1), dtype=torch.float32, device=self._q.device)
+        self._recv = torch.empty((self.world, rows, d + 1), dtype=torch.float32, device=self._q.device)
+        inv = c.rotation if self.rotate_back else None
+
+        def local():
+            if self.owner:
+                c._write(self._k, self._v)
+                c._advance_device(1)
+            o, s = c._decode(self._q, hq, extra=0, return_lse=True, full_capacity=True)
+            self._send[:, :d].copy_(o)
+            self._send[:, d].copy_(s)
+
+        def merge():
+            return ops.lse_merge(self._recv[..., :d], self._recv[..., d].contiguous(), inverse_rotation=inv)
+
+        # size the decode workspace and warm the collective outside capture
+        c._decode(self._q, hq, extra=0, return_lse=True, full_capacity=True)
+        self._gather()
         torch.cuda.synchronize()
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            self.graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph, stream=side):
-                if self.owner:
-                    c._write(self._k, self._v)
-                    c._advance_device(1)
-                o, s = c._decode(self._q, hq, extra=0, return_lse=True, full_capacity=True)
-                outs, lses = gather_partials(o, s, self.group)
-                self._out = ops.lse_merge(outs, lses, inverse_rotation=c.rotation if self.rotate_back else None)
+            self.g_local = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_local, stream=side, capture_error_mode="thread_local"):
+                local()
+            self.g_merge = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_merge, stream=side, capture_error_mode="thread_local"):
+                self._out = merge()
         torch.cuda.current_stream().wait_stream(side)
         assert self._out.shape == (rows, d)
 
+    def _gather(self) -> None:
+        if dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
+        else:
+            dist.all_gather(list(self._recv.unbind(0)), self._send, group=self.group)
+
     def step_graph(self):
-        """Replay the captured step (append the captured token, decode)."""
+        """One captured step: local graph, all-gather, merge graph.  Returns
+        the merged output (a static buffer, overwritten by the next step)."""
         if self.owner and self.cache.capacity - self.cache.sequence_length < 1:
             raise RuntimeError("cache capacity reached: capture again")
-        self.graph.replay()
+        self.g_local.replay()
+        self._gather()
+        self.g_merge.replay()
         if self.owner:
             self.cache._len_host += 1
         self.length += 1
         return self._out.reshape(self._qshape)
+
+    def release(self) -> None:
+        """Drop the captured graphs (call before destroying the process group)."""
+        self.g_local = self.g_merge = None
 
     def decode(self, query):
         """Full-sequence decode: local partial -> all-gather -> LSE merge."""
@@ -203,7 +234,7 @@ def run_sequence_split_bench(args, wl, rank: int, world: int) -> None:
     new_k = torch.randn((ring, 1, H, d), generator=gen, device=dev, dtype=torch.float16)
     new_v = torch.randn((ring, 1, H, d), generator=gen, device=dev, dtype=torch.float16)
     qs = torch.randn((ring, 1, Hq, d), generator=gen, device=dev, dtype=torch.float32)
-    dec.capture_step(new_k[0], new_v[0], qs[0])  # one CUDA graph per rank: append, decode, all-gather, merge
+    dec.capture_step(new_k[0], new_v[0], qs[0])  # per rank: local graph, all-gather, merge graph
     for _ in range(args.warmup):
         dec.step_graph()
     torch.cuda.synchronize()
@@ -233,10 +264,12 @@ def run_sequence_split_bench(args, wl, rank: int, world: int) -> None:
             "data": "synthetic (seeded fp16 N(0,1) K/V)",
             "config": {"workload": args.workload, "desc": wl["desc"], "global_batch": 1,
                        "parallelism": f"sequence-split x{world} + NCCL all-gather + LSE merge",
-                       "timing": "one CUDA graph per rank per step (append on the last rank, decode, all-gather, merge)"},
+                       "timing": "per rank per step: CUDA graph (append on the last rank + decode), NCCL all-gather, CUDA graph (merge)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None, "peak_kind": kind,
                          "note": "per-GPU packed bytes / whole step time (decode + all-gather + merge)"},
             "gpu_launches": 5 * args.steps,
         }), flush=True)
+    dec.release()
+    torch.cuda.synchronize()
     dist.destroy_process_group()
