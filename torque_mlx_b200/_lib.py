@@ -58,12 +58,15 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 _lib: ctypes.CDLL | None = None
+_cuda_ok = False  # a CUDA device was found once; the per-call check is skipped after that
 
 
 def load(require_cuda: bool = True) -> ctypes.CDLL:
     """Load the library (once).  ``require_cuda`` additionally demands a CUDA
     device, which every compute entry point needs."""
-    global _lib
+    global _lib, _cuda_ok
+    if _lib is not None and (_cuda_ok or not require_cuda):
+        return _lib
     if _lib is None:
         if not LIB_PATH.exists():
             raise RuntimeError(
@@ -75,8 +78,10 @@ def load(require_cuda: bool = True) -> ctypes.CDLL:
             fn.restype = res
             fn.argtypes = args
         _lib = lib
-    if require_cuda and not torch.cuda.is_available():
-        raise RuntimeError("torque_mlx_b200 needs a CUDA device (B200); none is available")
+    if require_cuda:
+        if not torch.cuda.is_available():
+            raise RuntimeError("torque_mlx_b200 needs a CUDA device (B200); none is available")
+        _cuda_ok = True
     return _lib
 
 
@@ -91,7 +96,13 @@ def check(status: int, what: str) -> None:
     raise exc(f"{what}: {msg}")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device | None = None) -> int:
+    """Handle of the current CUDA stream of ``device`` (default: current device)."""
+    if device is None and _raw_stream is not None:
+        return _raw_stream(torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 

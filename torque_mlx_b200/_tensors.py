@@ -18,15 +18,25 @@ def device() -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
+def _on_current_device(t: torch.Tensor) -> bool:
+    return t.is_cuda and t.device.index == torch.cuda.current_device()
+
+
 def is_numpy(x) -> bool:
     return not isinstance(x, torch.Tensor)
+
+
+_FLOATS = (torch.float16, torch.bfloat16, torch.float32)
 
 
 def to_cuda(x, dtype: torch.dtype | None = None, *, keep_half: bool = False) -> torch.Tensor:
     """Contiguous CUDA tensor.  ``keep_half`` keeps fp16/bf16 inputs as they are
     (the kernels widen them exactly); otherwise the result is ``dtype``."""
-    dev = device()
     if isinstance(x, torch.Tensor):
+        # fast path: already a usable tensor on the current device
+        if (x.is_contiguous() and (dtype is None or x.dtype == dtype or (keep_half and x.dtype in _FLOATS))
+                and _lib.load() is not None and _on_current_device(x)):
+            return x
         t = x
     else:
         a = np.asarray(x)
@@ -37,7 +47,7 @@ def to_cuda(x, dtype: torch.dtype | None = None, *, keep_half: bool = False) -> 
         pass
     elif dtype is not None and t.dtype != dtype:
         t = t.to(dtype)
-    return t.to(dev, non_blocking=False).contiguous()
+    return t.to(device(), non_blocking=False).contiguous()
 
 
 def words_to_cuda(x) -> torch.Tensor:

@@ -13,6 +13,7 @@
 //   * tensor — mma.sync m16n8k16 with fp16 operands (see tq_decode_mma.cuh).
 #include "tq_common.cuh"
 #include "tq_decode_mma.cuh"  // DecodeParams, kMma*
+#include "tq_merge.cuh"
 
 #include <math.h>
 #include <mutex>
@@ -20,8 +21,6 @@
 namespace tq {
 
 constexpr int kExactWarps = 4;
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 
 // ---------------------------------------------------------------------------
 // exact fp32 kernel
@@ -161,92 +160,22 @@ decode_exact_kernel(DecodeParams p) {
 // round-robin, so rows with many splits (long single sequences) merge in
 // parallel instead of one warp walking every part.
 // ---------------------------------------------------------------------------
+// Rows with many parts (a few long units split over every SM) merge with
+// 1024 threads a row, so each thread walks few parts; rows with a handful of
+// parts (batched decode) with 256.
 constexpr int kMergeWarps = 8;
-constexpr int kMergeMaxParts = 1024;  // parts weighed in shared memory per pass
+constexpr int kMergeWarpsWide = 32;
+constexpr int kMergeWideParts = 64;
 
-template <int D>
-__global__ void __launch_bounds__(kMergeWarps * 32)
+template <int D, int T>
+__global__ void __launch_bounds__(T)
 merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
                       float* __restrict__ out, float* __restrict__ lse, int inverse_rotate,
                       const float* __restrict__ signs_left, const float* __restrict__ signs_right) {
-  constexpr int E = D / 32;
-  constexpr int T = kMergeWarps * 32;
-  constexpr int SLICES = T / D;  // threads per output dim (parts split between them)
-  __shared__ float w_s[kMergeMaxParts];
-  __shared__ float acc_s[SLICES][D];
-  __shared__ float red[kMergeWarps];
-  __shared__ float sM, sL;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __shared__ float sm[MergeSmem<D, T>::FLOATS];
   const int64_t row = blockIdx.x;
-  const float* base = part + row * nparts * (int64_t)(D + 2);
-  const int np = nparts < kMergeMaxParts ? nparts : kMergeMaxParts;
-
-  // 1) max over parts that saw tokens (m is in log2 units)
-  float M = -INFINITY;
-  for (int i = tid; i < np; i += T) {
-    const float* pp = base + i * (int64_t)(D + 2);
-    if (pp[D + 1] > 0.f) M = fmaxf(M, pp[D]);
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
-  if (lane == 0) red[warp] = M;
-  __syncthreads();
-  if (tid == 0) {
-    float m = -INFINITY;
-    for (int w = 0; w < kMergeWarps; ++w) m = fmaxf(m, red[w]);
-    sM = m;
-  }
-  __syncthreads();
-  M = sM;
-  // 2) per-part weights 2^(m_i - M) (0 for empty parts) and the denominator
-  float L = 0.f;
-  for (int i = tid; i < np; i += T) {
-    const float* pp = base + i * (int64_t)(D + 2);
-    const float li = pp[D + 1];
-    const float w = (li > 0.f && M != -INFINITY) ? exp2f(pp[D] - M) : 0.f;
-    w_s[i] = w;
-    L += li * w;
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
-  __syncthreads();
-  if (lane == 0) red[warp] = L;
-  __syncthreads();
-  if (tid == 0) {
-    float l = 0.f;
-    for (int w = 0; w < kMergeWarps; ++w) l += red[w];
-    sL = l;
-  }
-  // 3) weighted sum: thread (slice, dim) sums parts slice, slice + SLICES, ...
-  //    with independent loads, four in flight
-  {
-    const int dim = tid % D, slice = tid / D;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    int i = slice;
-    for (; i + 3 * SLICES < np; i += 4 * SLICES) {
-      a0 = fmaf(base[(int64_t)i * (D + 2) + dim], w_s[i], a0);
-      a1 = fmaf(base[(int64_t)(i + SLICES) * (D + 2) + dim], w_s[i + SLICES], a1);
-      a2 = fmaf(base[(int64_t)(i + 2 * SLICES) * (D + 2) + dim], w_s[i + 2 * SLICES], a2);
-      a3 = fmaf(base[(int64_t)(i + 3 * SLICES) * (D + 2) + dim], w_s[i + 3 * SLICES], a3);
-    }
-    for (; i < np; i += SLICES) a0 = fmaf(base[(int64_t)i * (D + 2) + dim], w_s[i], a0);
-    acc_s[slice][dim] = (a0 + a1) + (a2 + a3);
-  }
-  __syncthreads();
-  if (warp != 0) return;
-  const float Lsum = sL;
-  float v[E];
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    float a = 0.f;
-#pragma unroll
-    for (int sl = 0; sl < SLICES; ++sl) a += acc_s[sl][j * 32 + lane];
-    v[j] = M == -INFINITY ? 0.f : a / Lsum;
-  }
-  if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
-#pragma unroll
-  for (int j = 0; j < E; ++j) out[row * D + j * 32 + lane] = v[j];
-  if (lse && lane == 0) lse[row] = (M == -INFINITY) ? -INFINITY : (M + log2f(Lsum)) * kLn2;
+  merge_row<D, T>(part + row * nparts * (int64_t)(D + 2), nparts, out + row * D, lse ? lse + row : nullptr,
+                  inverse_rotate, signs_left, signs_right, sm);
 }
 
 // ---------------------------------------------------------------------------
@@ -370,8 +299,12 @@ static void launch_decode_d(int bits, int mode, const DecodeParams& p, cudaStrea
 template <int D>
 static void launch_merge(const float* part, int nparts, int64_t rows, float* out, float* lse,
                          int inv, const float* sl, const float* sr, cudaStream_t st) {
-  merge_partials_kernel<D><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(part, nparts, rows, out, lse, inv,
-                                                                        sl, sr);
+  if (nparts >= kMergeWideParts)
+    merge_partials_kernel<D, kMergeWarpsWide * 32><<<(unsigned)rows, kMergeWarpsWide * 32, 0, st>>>(
+        part, nparts, rows, out, lse, inv, sl, sr);
+  else
+    merge_partials_kernel<D, kMergeWarps * 32><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(
+        part, nparts, rows, out, lse, inv, sl, sr);
 }
 
 }  // namespace tq

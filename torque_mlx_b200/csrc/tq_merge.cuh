@@ -1,0 +1,118 @@
+// Split-K merge of one query row: the partials (o_i un-normalised, m_i in
+// log2 units, l_i) of the row's parts become
+//     M = max m_i,  w_i = 2^(m_i - M),  L = sum w_i l_i,  o = sum w_i o_i / L
+// and, optionally, the inverse rotation; lse = (M + log2 L) ln 2.
+//
+// One CTA of T threads merges one row; the thread count is a template
+// parameter so rows with many parts (long single sequences split over every
+// SM) get more loads in flight.  The function starts and ends with a barrier
+// so calls can follow each other.
+#pragma once
+
+#include "tq_common.cuh"
+
+namespace tq {
+
+constexpr int kMergeMaxParts = 1024;  // parts weighed in shared memory per row
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Shared memory a merge_row call needs (floats): weights, per-slice sums,
+// per-warp reduction slots and the two row scalars.
+template <int D, int T>
+struct MergeSmem {
+  static constexpr int SLICES = T / D;  // threads per output dim (parts split between them)
+  static constexpr int FLOATS = kMergeMaxParts + T + T / 32 + 2;
+};
+
+// part row layout: [nparts][D + 2] = (o[0..D), m, l), read through L2
+// (ld.global.cg: every partial is read once).
+template <int D, int T>
+__device__ __forceinline__ void merge_row(const float* __restrict__ base, int nparts, float* __restrict__ out_row,
+                                          float* lse_row, int inverse_rotate, const float* signs_left,
+                                          const float* signs_right, float* smem) {
+  static_assert(T % D == 0 || D % T == 0, "thread count and head dim must nest");
+  static_assert(T >= D, "one thread per output dim at least");
+  constexpr int E = D / 32;
+  constexpr int NWARP = T / 32;
+  constexpr int SLICES = MergeSmem<D, T>::SLICES;
+  float* w_s = smem;                         // [kMergeMaxParts]
+  float* acc_s = w_s + kMergeMaxParts;       // [SLICES][D]
+  float* red = acc_s + T;                    // [NWARP]
+  float* row_s = red + NWARP;                // M, L
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int np = nparts < kMergeMaxParts ? nparts : kMergeMaxParts;
+  __syncthreads();  // smem may still be in use by the caller
+
+  // 1) max over parts that saw tokens
+  float M = -INFINITY;
+  for (int i = tid; i < np; i += T) {
+    const float* pp = base + i * (int64_t)(D + 2);
+    if (__ldcg(pp + D + 1) > 0.f) M = fmaxf(M, __ldcg(pp + D));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+  if (lane == 0) red[warp] = M;
+  __syncthreads();
+  if (tid == 0) {
+    float m = -INFINITY;
+    for (int w = 0; w < NWARP; ++w) m = fmaxf(m, red[w]);
+    row_s[0] = m;
+  }
+  __syncthreads();
+  M = row_s[0];
+  // 2) per-part weights (0 for empty parts) and the denominator
+  float L = 0.f;
+  for (int i = tid; i < np; i += T) {
+    const float* pp = base + i * (int64_t)(D + 2);
+    const float li = __ldcg(pp + D + 1);
+    const float w = (li > 0.f && M != -INFINITY) ? exp2f(__ldcg(pp + D) - M) : 0.f;
+    w_s[i] = w;
+    L += li * w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+  __syncthreads();  // every warp has read red[] (step 1) before it is reused
+  if (lane == 0) red[warp] = L;
+  __syncthreads();
+  if (tid == 0) {
+    float l = 0.f;
+    for (int w = 0; w < NWARP; ++w) l += red[w];
+    row_s[1] = l;
+  }
+  // 3) weighted sum: thread (slice, dim) sums parts slice, slice + SLICES, ...
+  //    with four independent loads in flight
+  {
+    const int dim = tid % D, slice = tid / D;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int i = slice;
+    for (; i + 3 * SLICES < np; i += 4 * SLICES) {
+      a0 = fmaf(__ldcg(base + (int64_t)i * (D + 2) + dim), w_s[i], a0);
+      a1 = fmaf(__ldcg(base + (int64_t)(i + SLICES) * (D + 2) + dim), w_s[i + SLICES], a1);
+      a2 = fmaf(__ldcg(base + (int64_t)(i + 2 * SLICES) * (D + 2) + dim), w_s[i + 2 * SLICES], a2);
+      a3 = fmaf(__ldcg(base + (int64_t)(i + 3 * SLICES) * (D + 2) + dim), w_s[i + 3 * SLICES], a3);
+    }
+    for (; i < np; i += SLICES) a0 = fmaf(__ldcg(base + (int64_t)i * (D + 2) + dim), w_s[i], a0);
+    acc_s[slice * D + dim] = (a0 + a1) + (a2 + a3);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const float Lsum = row_s[1];
+    float v[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      float a = 0.f;
+#pragma unroll
+      for (int sl = 0; sl < SLICES; ++sl) a += acc_s[sl * D + j * 32 + lane];
+      v[j] = M == -INFINITY ? 0.f : a / Lsum;
+    }
+    if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
+#pragma unroll
+    for (int j = 0; j < E; ++j) out_row[j * 32 + lane] = v[j];
+    if (lse_row && lane == 0) *lse_row = (M == -INFINITY) ? -INFINITY : (M + log2f(Lsum)) * kLn2;
+  }
+  __syncthreads();
+}
+
+
+}  // namespace tq

@@ -71,14 +71,24 @@ def decode_raw(*, query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tenso
                scale: float | None = None, mode: str | int = "auto", workspace: Workspace | None = None) -> None:
     """One ``tq_decode`` call on prepared device tensors (see include/torque_b200.h)."""
     lib = _lib.load()
-    ws = (workspace or _default_ws).get(workspace_bytes(units, group_size, head_dim, bits, max_len, mode), out.device)
+    wsp = workspace or _default_ws
     sl, sr = signs if signs is not None else (None, None)
-    _lib.check(lib.tq_decode(
-        query.data_ptr(), int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(), v_slab.data_ptr(),
-        unit_stride, _lib.ptr(lengths), units_per_seq, len_offset, max_len, units, group_size, head_dim, bits,
-        cent_k.data_ptr(), cent_v.data_ptr(), float(1.0 / sqrt(head_dim) if scale is None else scale),
-        out.data_ptr(), _lib.ptr(lse), int(inverse_rotate), decode_mode_code(mode), ws.data_ptr(), ws.numel(),
-        _lib.stream_ptr()), "decode")
+    args = [query.data_ptr(), int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(), v_slab.data_ptr(),
+            unit_stride, _lib.ptr(lengths), units_per_seq, len_offset, max_len, units, group_size, head_dim, bits,
+            cent_k.data_ptr(), cent_v.data_ptr(), float(1.0 / sqrt(head_dim) if scale is None else scale),
+            out.data_ptr(), _lib.ptr(lse), int(inverse_rotate), decode_mode_code(mode), None, 0, _lib.stream_ptr()]
+    ws = wsp.buf
+    if ws is not None and ws.device == out.device:
+        # the usual case: the current buffer is big enough and tq_decode
+        # launches straight away; a too-small one is refused before any launch
+        args[22], args[23] = ws.data_ptr(), ws.numel()
+        status = lib.tq_decode(*args)
+        if status != _lib.TQ_E_WORKSPACE:
+            _lib.check(status, "decode")
+            return
+    ws = wsp.get(workspace_bytes(units, group_size, head_dim, bits, max_len, mode), out.device)
+    args[22], args[23] = ws.data_ptr(), ws.numel()
+    _lib.check(lib.tq_decode(*args), "decode")
 
 
 def _cent(c) -> torch.Tensor:
