@@ -148,6 +148,32 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
               float* lse, int inverse_rotate_output, int mode, void* workspace,
               size_t workspace_bytes, tq_stream_t stream);
 
+/* One decode step with its append fused in: for every unit u of sequence
+ * s = u / units_per_seq, row u of new_k / new_v ([units, head_dim] in kv_dtype)
+ * is rotated (rotate_k / rotate_v), quantized with cent_k / cent_v and packed
+ * at position lengths[s] of the unit's slab rows, then the query attends
+ * tokens [0, lengths[s] + 1) exactly as tq_decode with len_offset = 1.  With
+ * advance = 1, lengths[s] += 1 once the step is complete (append + decode);
+ * with advance = 0 the lengths stay, which is the append-then-attend
+ * semantics of decode_mlx_with_current (cache_mlx.py:236-302): the token is
+ * written at the next position and attended but not counted, so a later
+ * append of the same token leaves the same cache.
+ * On the tensor-core path the CTA whose token chunk holds the new position
+ * packs the token itself before it loads its tiles, so a step is two kernel
+ * launches (decode + split merge) instead of four.  The caller guarantees
+ * lengths[s] + 1 <= max_len (rows past max_len are neither written nor
+ * attended) and the usual tq_decode workspace.
+ * Replaces the TorqueKVCacheMLX.append_many_mlx + decode_mlx pair of one
+ * generation step (cache_mlx.py:151-234) and decode_mlx_with_current. */
+int tq_decode_append(const void* new_k, const void* new_v, int kv_dtype, int rotate_k, int rotate_v,
+                     int advance, const float* query, int rotate_query, const float* signs_left,
+                     const float* signs_right, uint32_t* k_slab, uint32_t* v_slab,
+                     int64_t unit_stride_words, int32_t* lengths, int units_per_seq, int64_t max_len,
+                     int64_t units, int group_size, int head_dim, int bits, const float* cent_k,
+                     const float* cent_v, float scale, float* out, float* lse,
+                     int inverse_rotate_output, int mode, void* workspace, size_t workspace_bytes,
+                     tq_stream_t stream);
+
 /* Allocation-free variant of tq_decode.  No counterpart in the reference.
  *
  * For callers that cannot allocate device memory (or must not at this point):

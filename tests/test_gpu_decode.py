@@ -328,3 +328,84 @@ def test_many_units_wide_ctas(d, b):
                               value=rng.standard_normal((1, H, n, d)).astype(np.float16))
     q = rng.standard_normal((B, 1, H * G, d)).astype(np.float32)
     np.testing.assert_allclose(cache.decode(query=q), _oracle_for(cache, q), **TOL["tensor"])
+
+
+@pytest.mark.parametrize("mode", ["exact", "tensor"])
+@pytest.mark.parametrize("d,b", [(64, 2), (128, 3), (128, 4), (256, 4)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_append_decode_matches_append_then_decode(mode, d, b, dtype):
+    """tq_decode_append (token packed inside the decode kernel) leaves the same
+    packed words and returns the same output as tq_append_kv + tq_decode, for
+    ragged batches whose new tokens land at empty, chunk-edge and mid-chunk
+    positions."""
+    rng = np.random.default_rng(d * 10 + b)
+    B, L, H, G = 3, 2, 2, 4
+    cfg = T.TorqueConfig(bit_width=b, head_dim=d, num_layers=L, kv_heads=H)
+    fused = T.TorqueKVCache(config=cfg, batch_size=B, decode_mode=mode, initial_capacity=4096)
+    ref = T.TorqueKVCache(config=cfg, batch_size=B, decode_mode=mode, initial_capacity=4096)
+    for s, n in enumerate((0, 128, 2047)):
+        if n:
+            k = rng.standard_normal((L, H, n, d)).astype(np.float16)
+            v = rng.standard_normal((L, H, n, d)).astype(np.float16)
+            fused.append_sequence(s, key=k, value=v)
+            ref.append_sequence(s, key=k, value=v)
+    for step in range(3):
+        nk = torch.from_numpy(rng.standard_normal((B, L, H, d)).astype(np.float32)).to("cuda", dtype)
+        nv = torch.from_numpy(rng.standard_normal((B, L, H, d)).astype(np.float32)).to("cuda", dtype)
+        q = torch.from_numpy(rng.standard_normal((B, L, H * G, d)).astype(np.float32)).cuda()
+        got = fused.append_decode(key=nk, value=nv, query=q)
+        ref.append(key=nk, value=nv)
+        want = ref.decode(query=q)
+        np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), atol=1e-6, rtol=1e-6, err_msg=f"step {step}")
+        assert list(fused.lengths) == list(ref.lengths)
+        assert fused.device_lengths.cpu().tolist() == list(ref.lengths)
+    for a, c in zip(fused.packed_words(), ref.packed_words()):
+        np.testing.assert_array_equal(a, c)
+    np.testing.assert_allclose(fused.decode(query=q).cpu().numpy(), _oracle_for(fused, q.cpu().numpy()),
+                               **TOL[mode])
+
+
+def test_append_decode_rotation_flags():
+    """Fused append honours per-side rotation (keys rotated at run time,
+    values pre-rotated by folded weights) like the two-call path."""
+    rng = np.random.default_rng(5)
+    cfg = T.TorqueConfig(bit_width=4, head_dim=128, kv_heads=2, fused_weights=True)
+    kw = dict(config=cfg, rotate_keys_on_append=True, rotate_values_on_append=False, rotate_queries_on_decode=True,
+              initial_capacity=600)
+    fused, ref = T.TorqueKVCache(**kw), T.TorqueKVCache(**kw)
+    k = rng.standard_normal((2, 500, 128)).astype(np.float16)
+    v = rng.standard_normal((2, 500, 128)).astype(np.float16)
+    fused.append(key=k, value=v)
+    ref.append(key=k, value=v)
+    nk = rng.standard_normal((2, 128)).astype(np.float32)
+    nv = rng.standard_normal((2, 128)).astype(np.float32)
+    q = rng.standard_normal((8, 128)).astype(np.float32)
+    got = fused.append_decode(key=nk, value=nv, query=q)
+    ref.append(key=nk, value=nv)
+    np.testing.assert_allclose(got, ref.decode(query=q), atol=1e-6, rtol=1e-6)
+    for a, c in zip(fused.packed_words(), ref.packed_words()):
+        np.testing.assert_array_equal(a, c)
+
+
+@pytest.mark.parametrize("b", [3, 4])
+def test_append_decode_many_units(b):
+    """The 16-warp CTA path with the fused append (>= 2 units per SM)."""
+    rng = np.random.default_rng(b)
+    B, H, G, d = 40, 8, 4, 128
+    cfg = T.TorqueConfig(bit_width=b, head_dim=d, kv_heads=H)
+    fused = T.TorqueKVCache(config=cfg, batch_size=B, decode_mode="tensor", initial_capacity=512)
+    ref = T.TorqueKVCache(config=cfg, batch_size=B, decode_mode="tensor", initial_capacity=512)
+    for s, n in enumerate(rng.integers(0, 400, size=B)):
+        if n:
+            k = rng.standard_normal((1, H, n, d)).astype(np.float16)
+            v = rng.standard_normal((1, H, n, d)).astype(np.float16)
+            fused.append_sequence(s, key=k, value=v)
+            ref.append_sequence(s, key=k, value=v)
+    nk = torch.from_numpy(rng.standard_normal((B, 1, H, d)).astype(np.float16)).cuda()
+    nv = torch.from_numpy(rng.standard_normal((B, 1, H, d)).astype(np.float16)).cuda()
+    q = torch.from_numpy(rng.standard_normal((B, 1, H * G, d)).astype(np.float32)).cuda()
+    got = fused.append_decode(key=nk, value=nv, query=q)
+    ref.append(key=nk, value=nv)
+    np.testing.assert_allclose(got.cpu().numpy(), ref.decode(query=q).cpu().numpy(), atol=1e-6, rtol=1e-6)
+    for a, c in zip(fused.packed_words(), ref.packed_words()):
+        np.testing.assert_array_equal(a, c)

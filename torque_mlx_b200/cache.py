@@ -361,6 +361,52 @@ class TorqueKVCache:
 
     decode_mlx = decode
 
+    def _step(self, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor, hq: int, *, advance: bool, return_lse: bool,
+              full_capacity: bool = False, out: torch.Tensor | None = None):
+        """Fused append + decode of one token per sequence (tq_decode_append):
+        ``k``/``v`` are ``[B, L, H, 1, d]``; the token is packed at each
+        sequence's length and attended; ``advance`` counts it on the device
+        (the host copy of the lengths is the caller's to update)."""
+        cfg = self.config
+        self._ensure_capacity(int(self._len_host.max()) + 1)
+        if v.dtype != k.dtype:
+            v = v.to(k.dtype)
+        G = hq // cfg.kv_heads
+        units = self.batch_size * cfg.num_layers * cfg.kv_heads
+        if out is None:
+            out = torch.empty_like(q)
+        lse = torch.empty((q.shape[0],), dtype=torch.float32, device=q.device) if return_lse else None
+        max_len = self._cap if full_capacity else min(self._cap, int(self._len_host.max()) + 1)
+        ops.decode_append_raw(
+            new_k=k.reshape(units, cfg.head_dim), new_v=v.reshape(units, cfg.head_dim),
+            rotate_k=self.rotate_keys_on_append, rotate_v=self.rotate_values_on_append, advance=advance, query=q,
+            k_slab=self._k, v_slab=self._v, unit_stride=self._cap * self._W, lengths=self._len_dev,
+            units_per_seq=cfg.num_layers * cfg.kv_heads, max_len=max_len, units=units, group_size=G,
+            head_dim=cfg.head_dim, bits=cfg.bit_width, cent_k=self._ck, cent_v=self._cv, out=out, lse=lse,
+            rotate_query=self.rotate_queries_on_decode, inverse_rotate=not cfg.fused_weights, signs=self._signs,
+            scale=1.0 / sqrt(cfg.head_dim), mode=self.decode_mode, workspace=self._ws)
+        return out, lse
+
+    def append_decode(self, *, key, value, query, return_lse: bool = False):
+        """One generation step in one fused call: append one token to every
+        sequence (``key``/``value`` in ``append``'s single-token shapes) and
+        attend ``query`` over the cache including it.  Same result as
+        ``append`` followed by ``decode``, with the token packed inside the
+        decode kernel (tq_decode_append)."""
+        np_out = _tensors.is_numpy(query)
+        q, hq, out_shape = self._norm_query(query)
+        k = self._norm_kv(key, "key")
+        v = self._norm_kv(value, "value")
+        if k.shape[3] != 1 or v.shape[3] != 1:
+            raise ValueError("append_decode expects a single token per sequence for key/value")
+        out, lse = self._step(k, v, q, hq, advance=True, return_lse=return_lse)
+        self._len_host += 1
+        res = _tensors.out(out.reshape(out_shape), np_out)
+        if return_lse:
+            lse_shape = out_shape[:-1] if len(out_shape) > 1 else ()
+            return res, _tensors.out(lse.reshape(lse_shape), np_out)
+        return res
+
     def decode_with_current(self, *, query, key, value):
         """Attend the cache plus one current token that is not yet appended
         (cache_mlx.py:236-302): the token is packed at each sequence's next
@@ -372,8 +418,7 @@ class TorqueKVCache:
         v = self._norm_kv(value, "value")
         if k.shape[3] != 1 or v.shape[3] != 1:
             raise ValueError("decode_with_current expects a single current token for key/value")
-        self._write(k, v)
-        out, _ = self._decode(q, hq, extra=1, return_lse=False)
+        out, _ = self._step(k, v, q, hq, advance=False, return_lse=False)
         return _tensors.out(out.reshape(out_shape), np_out)
 
     decode_mlx_with_current = decode_with_current
@@ -426,9 +471,9 @@ TorqueKVCacheB200 = TorqueKVCache
 class CapturedDecodeStep:
     """One decode step of a TorqueKVCache replayed from CUDA graphs.
 
-    Two graphs: ``append`` (tq_append_kv + tq_lengths_add on the static key /
-    value buffers) and ``decode`` (tq_decode on the static query buffer into the
-    static output).  The decode plan covers the cache's whole capacity, so the
+    Three graphs over the static key / value / query buffers and the static
+    output: ``append`` (tq_append_kv + tq_lengths_add), ``decode`` (tq_decode)
+    and ``step`` (tq_decode_append: both in one decode launch plus the merge).  The decode plan covers the cache's whole capacity, so the
     captured launch stays valid as the device lengths grow; call ``step`` (or
     the two replays) until ``remaining`` reaches zero, then capture again.
     """
@@ -460,6 +505,10 @@ class CapturedDecodeStep:
             self.g_decode = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.g_decode, stream=stream):
                 cache._decode(self.query, hq, extra=0, return_lse=False, full_capacity=True, out=self.out)
+            self.g_step = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_step, stream=stream):
+                cache._step(self.key, self.value, self.query, hq, advance=True, return_lse=False,
+                            full_capacity=True, out=self.out)
         torch.cuda.current_stream(cache._dev).wait_stream(stream)
 
     @property
@@ -478,5 +527,10 @@ class CapturedDecodeStep:
         return self.out.reshape(self._out_shape)
 
     def step(self) -> torch.Tensor:
-        self.append()
-        return self.decode()
+        """Append the static token and attend, as one fused replay
+        (tq_decode_append: the decode kernel packs the token)."""
+        if self.remaining < 1:
+            raise RuntimeError("cache capacity reached: capture the step again")
+        self.g_step.replay()
+        self.cache._len_host += 1
+        return self.out.reshape(self._out_shape)

@@ -56,22 +56,7 @@ append_pack_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t gro
   for (int j = 0; j < E; ++j) val[j] = to_f32(src[j * 32 + lane]);
   if (rotate) warp_rotate<D>(val, lane, signs_right, signs_left);
 
-  uint32_t out_word = 0;
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    const uint32_t code = nearest_code<BITS>(val[j], c);
-    // 32 codes of group j fill BITS words; code of lane l starts at bit BITS*l.
-#pragma unroll
-    for (int q = 0; q < BITS; ++q) {
-      const int shift = BITS * lane - 32 * q;
-      uint32_t part = 0;
-      if (shift >= 0 && shift < 32) part = code << shift;
-      else if (shift < 0 && shift > -BITS) part = code >> (-shift);
-      const uint32_t word = __reduce_or_sync(FULL, part);
-      if (lane == j * BITS + q) out_word = word;
-    }
-  }
-  if (lane < W) slab[g * group_stride + pos * W + lane] = out_word;
+  warp_pack_row<D, BITS>(val, lane, c, slab + g * group_stride + pos * W);
 }
 
 // rotation only (RotationSpec.apply / inverse)

@@ -105,6 +105,40 @@ __device__ __forceinline__ uint32_t nearest_code(float x, const float (&c)[1 << 
   return best;
 }
 
+// Quantize a warp-resident row (v[j] = x[j*32 + lane]) against the
+// codebook c and store its W = D*BITS/32 packed words (LSB-first: code i at
+// bit i*BITS) to dst.  The 32 codes of register j fill words j*BITS ..
+// j*BITS + BITS-1; lane j*BITS + q assembles word q of group j with one
+// warp OR-reduction and lanes 0..W-1 store.
+template <int D, int BITS>
+__device__ __forceinline__ void warp_pack_row(const float (&v)[D / 32], int lane, const float (&c)[1 << BITS],
+                                              uint32_t* dst) {
+  constexpr int E = D / 32;
+  constexpr int W = D * BITS / 32;
+  uint32_t out_word = 0;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const uint32_t code = nearest_code<BITS>(v[j], c);
+#pragma unroll
+    for (int q = 0; q < BITS; ++q) {
+      const int shift = BITS * lane - 32 * q;
+      uint32_t part = 0;
+      if (shift >= 0 && shift < 32) part = code << shift;
+      else if (shift < 0 && shift > -BITS) part = code >> (-shift);
+      const uint32_t word = __reduce_or_sync(FULL, part);
+      if (lane == j * BITS + q) out_word = word;
+    }
+  }
+  if (lane < W) dst[lane] = out_word;
+}
+
+// Element i of a row of the given dtype (TQ_F32 / TQ_F16 / TQ_BF16).
+__device__ __forceinline__ float load_as_f32(const void* x, int dtype, int64_t i) {
+  if (dtype == TQ_F16) return __half2float(reinterpret_cast<const __half*>(x)[i]);
+  if (dtype == TQ_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+  return reinterpret_cast<const float*>(x)[i];
+}
+
 // Extract code `i` of a packed vector (LSB-first, may straddle two words).
 template <int BITS>
 __device__ __forceinline__ uint32_t code_at(const uint32_t* w, int i) {

@@ -167,15 +167,21 @@ constexpr int kMergeWarps = 8;
 constexpr int kMergeWarpsWide = 32;
 constexpr int kMergeWideParts = 64;
 
+// advance (nullable): lengths[0..advance_n) += 1 once the step's decode is
+// complete (tq_decode_append), so the lengths the decode read stay put while
+// it runs.
 template <int D, int T>
 __global__ void __launch_bounds__(T)
 merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
                       float* __restrict__ out, float* __restrict__ lse, int inverse_rotate,
-                      const float* __restrict__ signs_left, const float* __restrict__ signs_right) {
+                      const float* __restrict__ signs_left, const float* __restrict__ signs_right,
+                      int32_t* __restrict__ advance, int64_t advance_n) {
   __shared__ float sm[MergeSmem<D, T>::FLOATS];
   const int64_t row = blockIdx.x;
   merge_row<D, T>(part + row * nparts * (int64_t)(D + 2), nparts, out + row * D, lse ? lse + row : nullptr,
                   inverse_rotate, signs_left, signs_right, sm);
+  if (advance && row == 0)
+    for (int64_t i = threadIdx.x; i < advance_n; i += T) advance[i] += 1;
 }
 
 // ---------------------------------------------------------------------------
@@ -298,14 +304,25 @@ static void launch_decode_d(int bits, int mode, const DecodeParams& p, cudaStrea
 
 template <int D>
 static void launch_merge(const float* part, int nparts, int64_t rows, float* out, float* lse,
-                         int inv, const float* sl, const float* sr, cudaStream_t st) {
+                         int inv, const float* sl, const float* sr, int32_t* adv, int64_t adv_n,
+                         cudaStream_t st) {
   if (nparts >= kMergeWideParts)
     merge_partials_kernel<D, kMergeWarpsWide * 32><<<(unsigned)rows, kMergeWarpsWide * 32, 0, st>>>(
-        part, nparts, rows, out, lse, inv, sl, sr);
+        part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
   else
     merge_partials_kernel<D, kMergeWarps * 32><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(
-        part, nparts, rows, out, lse, inv, sl, sr);
+        part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
 }
+
+// The new token of a fused append-and-decode step (tq_decode_append).
+struct StepAppend {
+  const void* k;
+  const void* v;
+  int dtype;
+  int rotate_k, rotate_v;
+  int32_t* lengths;  // writable lengths (advanced by the merge when advance != 0)
+  int advance;
+};
 
 }  // namespace tq
 
@@ -324,13 +341,17 @@ int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int bi
   return TQ_OK;
 }
 
-int tq_decode(const float* query, int rotate_query, const float* signs_left,
-              const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
-              int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
-              int64_t len_offset, int64_t max_len, int64_t units, int group_size, int head_dim,
-              int bits, const float* cent_k, const float* cent_v, float scale, float* out,
-              float* lse, int inverse_rotate_output, int mode, void* workspace,
-              size_t workspace_bytes, tq_stream_t stream) {
+}  // extern "C"
+
+namespace tq {
+
+static int decode_core(const float* query, int rotate_query, const float* signs_left,
+                       const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
+                       int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
+                       int64_t len_offset, int64_t max_len, int64_t units, int group_size, int head_dim,
+                       int bits, const float* cent_k, const float* cent_v, float scale, float* out,
+                       float* lse, int inverse_rotate_output, int mode, void* workspace,
+                       size_t workspace_bytes, tq_stream_t stream, const StepAppend* app) {
   if (!valid_bits(bits)) return TQ_E_BITS;
   if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
   if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
@@ -373,8 +394,40 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
   p.nw = pl.nw;
   p.splits = pl.splits;
   p.part = (float*)workspace;
+  p.new_k = p.new_v = nullptr;
+  p.new_dtype = TQ_F32;
+  p.rotate_new_k = p.rotate_new_v = 0;
+  p.k_slab_w = p.v_slab_w = nullptr;
 
   cudaStream_t st = (cudaStream_t)stream;
+  if (app) {
+    if (pl.mode == TQ_DECODE_TENSOR) {
+      // packed inside the decode kernel by the CTA that owns the position
+      p.new_k = app->k;
+      p.new_v = app->v;
+      p.new_dtype = app->dtype;
+      p.rotate_new_k = app->rotate_k;
+      p.rotate_new_v = app->rotate_v;
+      p.k_slab_w = const_cast<uint32_t*>(k_slab);
+      p.v_slab_w = const_cast<uint32_t*>(v_slab);
+    } else {
+      // the exact kernel reads the token through the append kernel's output
+      uint32_t* ks = const_cast<uint32_t*>(k_slab);
+      uint32_t* vs = const_cast<uint32_t*>(v_slab);
+      int s0 = app->rotate_k == app->rotate_v
+                   ? tq_append_kv(app->k, app->v, app->dtype, units, 1, head_dim, bits, signs_left, signs_right,
+                                  app->rotate_k, cent_k, cent_v, ks, vs, unit_stride_words, max_len, lengths,
+                                  units_per_seq, len_offset - 1, stream)
+                   : tq_append_kv(app->k, nullptr, app->dtype, units, 1, head_dim, bits, signs_left, signs_right,
+                                  app->rotate_k, cent_k, cent_v, ks, vs, unit_stride_words, max_len, lengths,
+                                  units_per_seq, len_offset - 1, stream);
+      if (s0 == TQ_OK && app->rotate_k != app->rotate_v)
+        s0 = tq_append_kv(app->v, nullptr, app->dtype, units, 1, head_dim, bits, signs_left, signs_right,
+                          app->rotate_v, cent_v, cent_v, vs, vs, unit_stride_words, max_len, lengths,
+                          units_per_seq, len_offset - 1, stream);
+      if (s0 != TQ_OK) return s0;
+    }
+  }
   if (head_dim == 64) launch_decode_d<64>(bits, pl.mode, p, st);
   else if (head_dim == 128) launch_decode_d<128>(bits, pl.mode, p, st);
   else launch_decode_d<256>(bits, pl.mode, p, st);
@@ -383,10 +436,45 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
 
   const int nparts = pl.splits * pl.warps;
   const int64_t rows = units * group_size;
-  if (head_dim == 64) launch_merge<64>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, st);
-  else if (head_dim == 128) launch_merge<128>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, st);
-  else launch_merge<256>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, st);
+  int32_t* adv = (app && app->advance) ? app->lengths : nullptr;
+  const int64_t adv_n = units / (units_per_seq > 0 ? units_per_seq : 1);
+  if (head_dim == 64) launch_merge<64>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
+  else if (head_dim == 128) launch_merge<128>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
+  else launch_merge<256>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
   return launch_status();
+}
+
+}  // namespace tq
+
+extern "C" {
+
+int tq_decode(const float* query, int rotate_query, const float* signs_left,
+              const float* signs_right, const uint32_t* k_slab, const uint32_t* v_slab,
+              int64_t unit_stride_words, const int32_t* lengths, int units_per_seq,
+              int64_t len_offset, int64_t max_len, int64_t units, int group_size, int head_dim,
+              int bits, const float* cent_k, const float* cent_v, float scale, float* out,
+              float* lse, int inverse_rotate_output, int mode, void* workspace,
+              size_t workspace_bytes, tq_stream_t stream) {
+  return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
+                     units_per_seq, len_offset, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale,
+                     out, lse, inverse_rotate_output, mode, workspace, workspace_bytes, stream, nullptr);
+}
+
+int tq_decode_append(const void* new_k, const void* new_v, int kv_dtype, int rotate_k, int rotate_v,
+                     int advance, const float* query, int rotate_query, const float* signs_left,
+                     const float* signs_right, uint32_t* k_slab, uint32_t* v_slab,
+                     int64_t unit_stride_words, int32_t* lengths, int units_per_seq, int64_t max_len,
+                     int64_t units, int group_size, int head_dim, int bits, const float* cent_k,
+                     const float* cent_v, float scale, float* out, float* lse,
+                     int inverse_rotate_output, int mode, void* workspace, size_t workspace_bytes,
+                     tq_stream_t stream) {
+  if (!new_k || !new_v || !lengths) return TQ_E_ARG;
+  if (kv_dtype != TQ_F32 && kv_dtype != TQ_F16 && kv_dtype != TQ_BF16) return TQ_E_ARG;
+  if ((rotate_k || rotate_v) && (!signs_left || !signs_right)) return TQ_E_ARG;
+  StepAppend app{new_k, new_v, kv_dtype, rotate_k, rotate_v, lengths, advance};
+  return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
+                     units_per_seq, 1, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale, out, lse,
+                     inverse_rotate_output, mode, workspace, workspace_bytes, stream, &app);
 }
 
 int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, int head_dim,

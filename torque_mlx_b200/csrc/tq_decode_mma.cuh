@@ -57,7 +57,43 @@ struct DecodeParams {
   int nw;                // warps per CTA of the tensor-core kernel (kMmaWarps or kMmaWarpsWide)
   int splits;            // CTAs per unit
   float* part;           // [units*G, splits*(partials per CTA), D+2]
+  // fused append of one new token per unit (tq_decode_append); new_k == null: none.
+  // Row u of new_k / new_v is packed at position n_u - 1 of unit u, where
+  // n_u = lengths[seq] + len_offset before clamping (len_offset = 1).
+  const void* new_k;
+  const void* new_v;
+  int new_dtype;         // tq_dtype of new_k / new_v
+  int rotate_new_k;
+  int rotate_new_v;
+  uint32_t* k_slab_w;    // writable views of k_slab / v_slab
+  uint32_t* v_slab_w;
 };
+
+// Length of unit u before clamping to max_len.
+__device__ __forceinline__ int64_t unit_length_raw(const DecodeParams& p, int64_t u) {
+  int64_t n = p.len_offset;
+  if (p.lengths) n += p.lengths[u / p.units_per_seq];
+  return n;
+}
+
+// Pack unit u's new K (which = 0) or V (which = 1) row at position pos with
+// one warp: load, optional rotation, nearest centroid, LSB-first packing -
+// the append kernel's row path.
+template <int D, int BITS>
+__device__ __forceinline__ void append_new_row(const DecodeParams& p, int64_t u, int64_t pos, int which, int lane) {
+  constexpr int E = D / 32;
+  constexpr int W = D * BITS / 32;
+  const void* src = which ? p.new_v : p.new_k;
+  const float* cent = which ? p.cent_v : p.cent_k;
+  float c[1 << BITS];
+#pragma unroll
+  for (int i = 0; i < (1 << BITS); ++i) c[i] = __ldg(cent + i);
+  float v[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = load_as_f32(src, p.new_dtype, u * D + j * 32 + lane);
+  if (which ? p.rotate_new_v : p.rotate_new_k) warp_rotate<D>(v, lane, p.signs_right, p.signs_left);
+  warp_pack_row<D, BITS>(v, lane, c, (which ? p.v_slab_w : p.k_slab_w) + u * p.unit_stride + pos * W);
+}
 
 __device__ __forceinline__ int64_t unit_length(const DecodeParams& p, int64_t u) {
   int64_t n = p.len_offset;
@@ -148,6 +184,18 @@ struct Run {
   static constexpr int RAW = ALIGNED ? NW : NW + 1;
 };
 
+// Code words are streamed once, so they are read through L2 only
+// (ld.global.cg); that path is also coherent with the in-kernel append of
+// the step's new token, whose words the same CTA reads after a barrier.
+template <typename T>
+__device__ __forceinline__ T load_code(const T* p) {
+#if defined(TQ_CODE_LOADS_NC)
+  return __ldg(p);
+#else
+  return __ldcg(p);
+#endif
+}
+
 template <int NB, int W>
 __device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const uint32_t* row, int start) {
   constexpr int NW = Run<NB>::NW;
@@ -156,21 +204,21 @@ __device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const ui
 #pragma unroll
     for (int i = 0; i < NW; i += VEC) {
       if constexpr (VEC == 4) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(row + i));
+        const uint4 v = load_code(reinterpret_cast<const uint4*>(row + i));
         raw[i] = v.x; raw[i + 1] = v.y; raw[i + 2] = v.z; raw[i + 3] = v.w;
       } else if constexpr (VEC == 2) {
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(row + i));
+        const uint2 v = load_code(reinterpret_cast<const uint2*>(row + i));
         raw[i] = v.x; raw[i + 1] = v.y;
       } else {
-        raw[i] = __ldg(row + i);
+        raw[i] = load_code(row + i);
       }
     }
   } else {
     const bool tail = start + NB > 32 * NW;  // the run reaches one more word
 #pragma unroll
-    for (int i = 0; i < NW; ++i) raw[i] = __ldg(row + i);
+    for (int i = 0; i < NW; ++i) raw[i] = load_code(row + i);
     raw[NW] = 0u;
-    if (tail) raw[NW] = __ldg(row + NW);
+    if (tail) raw[NW] = load_code(row + NW);
   }
 }
 
@@ -448,6 +496,15 @@ decode_mma_kernel(DecodeParams p) {
     if (tile0 + 16 <= n) load_tile<D, BITS>(t, k, v, lp);
     else load_tile_clamped<D, BITS>(t, k, v, (int)(n - 1 - tile0), gr, tq, lp);
   };
+  // fused append: the CTA whose chunk holds the new token packs it first
+  if (p.new_k) {
+    const int64_t raw_n = unit_length_raw(p, u);
+    const int64_t pos = raw_n - 1;
+    if (raw_n >= 1 && raw_n <= p.max_len && pos >= c0 && pos < c0 + p.chunk) {
+      if (warp < 2) append_new_row<D, BITS>(p, u, pos, warp, lane);
+      __syncthreads();  // the new words are visible to the CTA's tile loads
+    }
+  }
   TileRegs<D, BITS> ta, tb;
   if (w0 < w1) fetch(ta, w0);
 

@@ -5,8 +5,8 @@ A plain pre-norm decoder (RMSNorm, RoPE, SwiGLU MLP, bf16 weights drawn from
 N(0, 0.02)) with one ``TorqueKVCache`` per layer.  Projections, norms and the
 MLP are ordinary cuBLAS / torch ops; the KV path is this library: prompt
 tokens are packed in bulk after a dense causal prefill, each generated token
-is appended (tq_append_kv) and attended straight on the packed codes
-(tq_decode).  The whole per-token step can be captured in one CUDA graph.
+is packed and attended straight on the packed codes in one fused call
+(tq_decode_append).  The whole per-token step can be captured in one CUDA graph.
 
 Rotation folding (reference: src/torque_mlx/conversion.py:19-51 and the Qwen
 adapter's runtime rotation, families/qwen.py:521-528, qwen_mlx.py:758-760):
@@ -164,13 +164,11 @@ class PackedKVDecoder:
             k = self._rope(k.reshape(Hkv, 1, d), cos, sin)
             v = v.reshape(Hkv, 1, d)
             if captured:
-                cache._write(k[None, None].reshape(1, 1, Hkv, 1, d), v.reshape(1, 1, Hkv, 1, d))
-                cache._advance_device(1)
-                qf = q.float().contiguous()
-                att = cache._decode(qf, H, extra=0, return_lse=False, full_capacity=True)[0]
+                # one fused launch packs the token and attends (tq_decode_append)
+                att = cache._step(k.reshape(1, 1, Hkv, 1, d), v.reshape(1, 1, Hkv, 1, d), q.float().contiguous(), H,
+                                  advance=True, return_lse=False, full_capacity=True)[0]
             else:
-                cache.append(key=k, value=v)
-                att = cache.decode(query=q.float())
+                att = cache.append_decode(key=k.reshape(Hkv, d), value=v.reshape(Hkv, d), query=q.float())
             x = x + att.reshape(1, H * d).to(x.dtype) @ lay["wo"].T
             x = x + self._mlp(self._rms(x, lay["mlp_norm"]), lay)
         self.pos.add_(1)

@@ -91,6 +91,36 @@ def decode_raw(*, query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tenso
     _lib.check(lib.tq_decode(*args), "decode")
 
 
+def decode_append_raw(*, new_k: torch.Tensor, new_v: torch.Tensor, rotate_k: bool, rotate_v: bool, advance: bool,
+                      query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tensor, unit_stride: int,
+                      lengths: torch.Tensor, units_per_seq: int, max_len: int, units: int, group_size: int,
+                      head_dim: int, bits: int, cent_k: torch.Tensor, cent_v: torch.Tensor, out: torch.Tensor,
+                      lse: torch.Tensor | None = None, rotate_query: bool = False, inverse_rotate: bool = False,
+                      signs: tuple[torch.Tensor, torch.Tensor] | None = None, scale: float | None = None,
+                      mode: str | int = "auto", workspace: Workspace | None = None) -> None:
+    """One ``tq_decode_append`` call: pack row u of ``new_k`` / ``new_v``
+    ([units, head_dim]) at its sequence's length, attend up to and including
+    it, and (``advance``) count it (see include/torque_b200.h)."""
+    lib = _lib.load()
+    wsp = workspace or _default_ws
+    sl, sr = signs if signs is not None else (None, None)
+    args = [new_k.data_ptr(), new_v.data_ptr(), _lib.dtype_code(new_k.dtype), int(rotate_k), int(rotate_v),
+            int(advance), query.data_ptr(), int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(),
+            v_slab.data_ptr(), unit_stride, lengths.data_ptr(), units_per_seq, max_len, units, group_size, head_dim,
+            bits, cent_k.data_ptr(), cent_v.data_ptr(), float(1.0 / sqrt(head_dim) if scale is None else scale),
+            out.data_ptr(), _lib.ptr(lse), int(inverse_rotate), decode_mode_code(mode), None, 0, _lib.stream_ptr()]
+    ws = wsp.buf
+    if ws is not None and ws.device == out.device:
+        args[27], args[28] = ws.data_ptr(), ws.numel()
+        status = lib.tq_decode_append(*args)
+        if status != _lib.TQ_E_WORKSPACE:
+            _lib.check(status, "decode_append")
+            return
+    ws = wsp.get(workspace_bytes(units, group_size, head_dim, bits, max_len, mode), out.device)
+    args[27], args[28] = ws.data_ptr(), ws.numel()
+    _lib.check(lib.tq_decode_append(*args), "decode_append")
+
+
 def _cent(c) -> torch.Tensor:
     if isinstance(c, Codebook):
         c = c.centroids
