@@ -4,11 +4,11 @@
 
 One step = one decode step of the workload: every sequence appends one new
 token (rotate + quantize + pack of K and V for all kv heads) and attends all
-query heads over its packed cache.  Default workload = BASELINE config 4:
+query heads over its packed cache.  Default workload = benchmark config 4:
 batch 64 per GPU, 32 query / 8 kv heads, head_dim 128, 3-bit codes, lengths
 U{16384..32768} (seeded), fp16 N(0,1) K/V.  Multi-GPU runs shard the batch
 (each rank owns 64 sequences; weak scaling, no collective on the data path).
-``--workload config3`` runs BASELINE config 3 (batch 1, 16/2 heads, d 256,
+``--workload config3`` runs benchmark config 3 (batch 1, 16/2 heads, d 256,
 4-bit, 131072-token context; N>1 splits the sequence across ranks and merges
 with an NCCL all-gather + LSE merge).
 

@@ -213,6 +213,30 @@ int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, 
                  float* out, float* lse_out, int inverse_rotate, const float* signs_left,
                  const float* signs_right, tq_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Decoder glue for the end-to-end generation step (benchmark config 5, a 28-layer GQA decoder).  No
+ * counterpart in the reference's C surface: these replace the PyTorch
+ * elementwise ops around the KV step of the example decoder (the reference
+ * runs the same ops as MLX graph nodes in its Qwen adapter,
+ * families/qwen_mlx.py).  bf16 tensors, fp32 math, bf16 rounding where the
+ * PyTorch ops round.
+ * ------------------------------------------------------------------------- */
+
+/* y[r] = bf16(bf16(x[r] * rsqrt(mean(x[r]^2) + eps)) * weight) for rows r of n
+ * (n even; 4-byte aligned pointers). */
+int tq_rmsnorm(const void* x, const void* weight, float eps, int64_t rows, int n, void* y, tq_stream_t stream);
+
+/* RoPE (interleaved pairs (2i, 2i+1), angle table rows at *position) on the
+ * q and k heads of one fused row qkv = [q_heads | kv_heads | kv_heads] x
+ * head_dim (bf16): q_out gets the bf16-rounded q in fp32, k_out the k heads
+ * in bf16.  cos/sin tables are [positions, head_dim/2] fp32; position is a
+ * device int64 (so a captured graph follows it). */
+int tq_rope_qk(const void* qkv, const float* cos_table, const float* sin_table, const int64_t* position,
+               int q_heads, int kv_heads, int head_dim, float* q_out, void* k_out, tq_stream_t stream);
+
+/* y[r, j] = bf16(bf16(silu(g)) * u) with g = gate_up[r, j], u = gate_up[r, f + j]. */
+int tq_silu_mul(const void* gate_up, int64_t rows, int f, void* y, tq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -68,7 +68,7 @@ def test_config1_small_matches_reference_cache(golden):
 
 @pytest.mark.parametrize("mode", ["exact", "tensor"])
 def test_config1_full_matches_reference(golden, mode):
-    """512 tokens, d 128, 8 heads, 4-bit, seed 0."""
+    """Benchmark config 1: 512 tokens, d 128, 8 heads, 4-bit, seed 0."""
     rng = np.random.default_rng(0)
     keys = rng.standard_normal((512, 8, 128)).astype(np.float16)
     vals = rng.standard_normal((512, 8, 128)).astype(np.float16)

@@ -1,4 +1,4 @@
-"""End-to-end decoder on the packed cache (BASELINE config 5 geometry, scaled
+"""End-to-end decoder on the packed cache (benchmark config 5 geometry, scaled
 down): eager and CUDA-graph steps agree, and one decode step's attention equals
 dense attention over the cache's own dequantized K/V."""
 

@@ -57,6 +57,10 @@ SIGNATURES: dict[str, tuple] = {
     "tq_decode_static": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
                                  c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
                                  c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "tq_rmsnorm": (c_int, [c_void_p, c_void_p, c_float, c_int64, c_int, c_void_p, c_void_p]),
+    "tq_rope_qk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
+                           c_void_p]),
+    "tq_silu_mul": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "tq_lse_merge": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p,
                              c_void_p, c_void_p]),
 }

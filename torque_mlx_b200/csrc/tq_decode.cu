@@ -261,14 +261,21 @@ static Plan make_plan(int64_t units, int G, int D, int bits, int64_t max_len, in
   pl.mode = resolve_mode(mode, G);
   pl.warps = pl.mode == TQ_DECODE_TENSOR ? 1 : kExactWarps;  // partials per CTA
   const int sms = sm_count();
-  // batched decode (at least two units per SM): 16-warp CTAs; few long units: 8-warp CTAs
-  pl.nw = (pl.mode == TQ_DECODE_TENSOR && D <= 128 && units >= 2 * (int64_t)sms) ? kMmaWarpsWide : kMmaWarps;
+  // d <= 128: 16-warp CTAs (one per SM, the pair tables built once per SM)
+  // for batched decode (at least two units per SM) and for a few long units
+  // (at most SMs/8, each split over >= 8 SMs); in between, 8-warp CTAs (two
+  // per SM) spread the units over more SMs.
+  const bool wide_ok = pl.mode == TQ_DECODE_TENSOR && D <= 128;
+  pl.nw = (wide_ok && (units >= 2 * (int64_t)sms || units * 8 <= (int64_t)sms)) ? kMmaWarpsWide : kMmaWarps;
   const int tile = pl.mode == TQ_DECODE_TENSOR ? pl.nw * 16 : kExactWarps * 32;
   const int per_sm = pl.mode == TQ_DECODE_TENSOR ? mma_blocks_per_sm(D, bits, G, pl.nw) : 4;
   const int64_t wave = (int64_t)sms * per_sm;
   const int64_t len = max_len < 1 ? 1 : max_len;
   const int64_t uu = units < 1 ? 1 : units;
-  int64_t splits = uu < wave ? (wave + uu - 1) / uu : (4 * wave + uu - 1) / uu;
+  // few units: as many splits as keep every unit's CTAs inside one wave
+  // (rounding up would leave a nearly empty second wave); many units: about
+  // four waves of CTAs so the ragged tails even out
+  int64_t splits = uu < wave ? wave / uu : (4 * wave + uu - 1) / uu;
   const int64_t max_splits = (len + tile - 1) / tile;
   if (splits > max_splits) splits = max_splits;
   if (splits * pl.warps > kMergeMaxParts) splits = kMergeMaxParts / pl.warps;  // merge weighs parts in smem

@@ -102,8 +102,9 @@ __device__ __forceinline__ int64_t unit_length(const DecodeParams& p, int64_t u)
   return n < 0 ? 0 : n;
 }
 
-// Warps per CTA: 8 (two CTAs per SM) for few, long units; 16 (one CTA per SM,
-// the tables built once for 16 warps) for batched decode with many units.
+// Warps per CTA: 16 (one CTA per SM, the tables built once for 16 warps) for
+// batched decode and for a few long units; 8 (two CTAs per SM) in between
+// and for d = 256.
 constexpr int kMmaWarps = 8;
 constexpr int kMmaWarpsWide = 16;
 constexpr float kLazyMaxSlack = 8.f;              // log2 headroom before the max is raised

@@ -1,5 +1,5 @@
 """Random-init GQA decoder whose attention runs on the packed rotated KV cache
-(the model-side glue of SURVEY §8f row 1).
+(benchmark config 5: the model around the packed-KV path).
 
 A plain pre-norm decoder (RMSNorm, RoPE, SwiGLU MLP, bf16 weights drawn from
 N(0, 0.02)) with one ``TorqueKVCache`` per layer.  Projections, norms and the
@@ -11,7 +11,7 @@ is packed and attended straight on the packed codes in one fused call
 Rotation folding (reference: src/torque_mlx/conversion.py:19-51 and the Qwen
 adapter's runtime rotation, families/qwen.py:521-528, qwen_mlx.py:758-760):
 
-* ``fold="full"``: Pi folded into W_Q, W_K, W_V and Pi^T into W_O, as BASELINE
+* ``fold="full"``: Pi folded into W_Q, W_K, W_V and Pi^T into W_O, as benchmark
   config 5 specifies.  RoPE then acts on rotated q/k, which is a different
   (self-consistent) model from the unfolded one, since Pi and RoPE do not
   commute; for random weights that is immaterial.
@@ -27,6 +27,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import ops
 from .cache import TorqueKVCache
 from .config import TorqueConfig
 from .rotation import RotationSpec
@@ -90,6 +91,8 @@ class PackedKVDecoder:
         ang = torch.arange(max_tokens + 1, device=self.dev, dtype=torch.float32)[:, None] * inv[None]
         self.cos, self.sin = ang.cos(), ang.sin()  # [pos, d/2]
         self.pos = torch.zeros((), dtype=torch.long, device=self.dev)  # next position (device, for graphs)
+        self._qf = torch.empty((cfg.q_heads, d), dtype=torch.float32, device=self.dev)  # roped q of the step
+        self._kr = torch.empty((cfg.kv_heads, d), dtype=bf, device=self.dev)         # roped k of the step
         self.length = 0
         self.graph = None
 
@@ -150,29 +153,31 @@ class PackedKVDecoder:
 
     # -- one generated token --------------------------------------------------------
     def _step_body(self, token: torch.Tensor, captured: bool) -> torch.Tensor:
+        """One token through every layer: tq_rmsnorm, the qkv GEMM, tq_rope_qk,
+        the fused packed-KV step, the output GEMM with the residual folded in
+        (addmm), tq_rmsnorm, gate/up GEMM, tq_silu_mul and the down GEMM with
+        the residual: ten launches a layer."""
         cfg = self.cfg
         H, Hkv, d = cfg.q_heads, cfg.kv_heads, cfg.head_dim
-        # index_select keeps the lookups on the device (graph-safe, no host sync)
+        # index_select keeps the lookup on the device (graph-safe, no host sync)
         x = torch.index_select(self.embed, 0, token.reshape(1))
-        p = self.pos.reshape(1)
-        cos, sin = torch.index_select(self.cos, 0, p), torch.index_select(self.sin, 0, p)
+        qf, kr = self._qf, self._kr
         for lay, cache in zip(self.layers, self.caches):
-            h = self._rms(x, lay["attn_norm"])
+            h = ops.rmsnorm(x, lay["attn_norm"], cfg.rms_eps)
             qkv = h @ lay["wqkv"].T
-            q, k, v = qkv.split([H * d, Hkv * d, Hkv * d], dim=-1)
-            q = self._rope(q.reshape(H, 1, d), cos, sin).reshape(H, d)
-            k = self._rope(k.reshape(Hkv, 1, d), cos, sin)
-            v = v.reshape(Hkv, 1, d)
+            ops.rope_qk(qkv, self.cos, self.sin, self.pos, H, Hkv, d, qf, kr)
+            v = qkv[:, (H + Hkv) * d:]
             if captured:
                 # one fused launch packs the token and attends (tq_decode_append)
-                att = cache._step(k.reshape(1, 1, Hkv, 1, d), v.reshape(1, 1, Hkv, 1, d), q.float().contiguous(), H,
+                att = cache._step(kr.reshape(1, 1, Hkv, 1, d), v.reshape(1, 1, Hkv, 1, d), qf, H,
                                   advance=True, return_lse=False, full_capacity=True)[0]
             else:
-                att = cache.append_decode(key=k.reshape(Hkv, d), value=v.reshape(Hkv, d), query=q.float())
-            x = x + att.reshape(1, H * d).to(x.dtype) @ lay["wo"].T
-            x = x + self._mlp(self._rms(x, lay["mlp_norm"]), lay)
+                att = cache.append_decode(key=kr, value=v.reshape(Hkv, d), query=qf)
+            x = torch.addmm(x, att.reshape(1, H * d).to(x.dtype), lay["wo"].T)
+            h = ops.rmsnorm(x, lay["mlp_norm"], cfg.rms_eps)
+            x = torch.addmm(x, ops.silu_mul(h @ lay["w_gate_up"].T), lay["w_down"].T)
         self.pos.add_(1)
-        return self._rms(x, self.final_norm) @ self.lm_head.T
+        return ops.rmsnorm(x, self.final_norm, cfg.rms_eps) @ self.lm_head.T
 
     @torch.no_grad()
     def step(self, token: torch.Tensor) -> torch.Tensor:

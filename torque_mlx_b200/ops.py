@@ -293,3 +293,48 @@ def dequantize_packed(words, codebook, *, bit_width: int, head_dim: int):
 
 def as_numpy_words(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().view(torch.int32).cpu().numpy().view(np.uint32)
+
+
+# ---------------------------------------------------------------------------
+# decoder glue (tq_rmsnorm / tq_rope_qk / tq_silu_mul): bf16 in and out
+# ---------------------------------------------------------------------------
+def _bf16_rows(x: torch.Tensor, name: str) -> torch.Tensor:
+    if x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    return x
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-wise RMSNorm over the last axis: bf16(bf16(x * rsqrt(mean(x^2) + eps)) * weight)."""
+    lib = _lib.load()
+    _bf16_rows(x, "x")
+    _bf16_rows(weight, "weight")
+    n = x.shape[-1]
+    out = torch.empty_like(x) if out is None else out
+    _lib.check(lib.tq_rmsnorm(x.data_ptr(), weight.data_ptr(), float(eps), x.numel() // n, n, out.data_ptr(),
+                              _lib.stream_ptr()), "rmsnorm")
+    return out
+
+
+def rope_qk(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, position: torch.Tensor, q_heads: int,
+            kv_heads: int, head_dim: int, q_out: torch.Tensor, k_out: torch.Tensor) -> None:
+    """RoPE on the q and k heads of one fused qkv row at the device position
+    ``position`` (int64 scalar tensor): q_out [q_heads, d] fp32 (bf16 values),
+    k_out [kv_heads, d] bf16."""
+    lib = _lib.load()
+    _bf16_rows(qkv, "qkv")
+    if position.dtype != torch.int64 or q_out.dtype != torch.float32 or k_out.dtype != torch.bfloat16:
+        raise ValueError("rope_qk: position int64, q_out fp32 and k_out bf16 expected")
+    _lib.check(lib.tq_rope_qk(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), position.data_ptr(), q_heads, kv_heads,
+                              head_dim, q_out.data_ptr(), k_out.data_ptr(), _lib.stream_ptr()), "rope_qk")
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU activation of rows [gate | up]: bf16(bf16(silu(gate)) * up)."""
+    lib = _lib.load()
+    _bf16_rows(gate_up, "gate_up")
+    f = gate_up.shape[-1] // 2
+    rows = gate_up.numel() // (2 * f)
+    out = torch.empty(gate_up.shape[:-1] + (f,), dtype=torch.bfloat16, device=gate_up.device) if out is None else out
+    _lib.check(lib.tq_silu_mul(gate_up.data_ptr(), rows, f, out.data_ptr(), _lib.stream_ptr()), "silu_mul")
+    return out

@@ -2,11 +2,11 @@
 
 The reference runs on one device only; these partitions are new.
 
-* Batch sharding: each rank owns whole sequences and runs
+* Batch sharding (benchmark config 4): each rank owns whole sequences and runs
   the unchanged single-GPU step; there is no collective on the data path.
   ``shard_batch`` gives the rank's slice.
 
-* Sequence sharding (long batch-1 contexts): each rank
+* Sequence sharding (benchmark config 3, long batch-1 contexts): each rank
   owns a contiguous share of the prefill tokens plus the new tokens it is
   assigned (round robin, or all on the last rank for graph-captured steps).  A decode step is
       local tq_decode over the rank's tokens -> (o_r rotated, lse_r)
