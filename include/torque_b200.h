@@ -237,6 +237,17 @@ int tq_rope_qk(const void* qkv, const float* cos_table, const float* sin_table, 
 /* y[r, j] = bf16(bf16(silu(g)) * u) with g = gate_up[r, j], u = gate_up[r, f + j]. */
 int tq_silu_mul(const void* gate_up, int64_t rows, int f, void* y, tq_stream_t stream);
 
+/* One-token linear layer: y[i] = bf16(sum_j weight[i, j] x'[j] (+ residual[i]))
+ * for weight [n, k] bf16 (16-byte aligned, k a multiple of 256, k <= 8192),
+ * fp32 accumulation, where x' is built from x by x_mode:
+ *   0  x' = x (bf16 [k])
+ *   1  x' = bf16(x) (fp32 [k])
+ *   2  x' = tq_rmsnorm(x, norm_weight, eps) (bf16 [k])
+ *   3  x' = tq_silu_mul(x) (bf16 [2k] = [gate | up])
+ * residual (nullable) is bf16 [n], added in fp32 before the one rounding. */
+int tq_gemv(const void* weight, const void* x, int x_mode, const void* norm_weight, float eps,
+            const void* residual, void* y, int n, int k, tq_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

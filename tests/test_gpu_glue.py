@@ -99,3 +99,31 @@ def test_glue_step_matches_torch_step():
         scale = float(want.abs().max())
         assert float((got - want).abs().max()) <= 0.03 * scale, (float((got - want).abs().max()), scale)
         tok = want.argmax(-1).reshape(())
+
+
+@pytest.mark.parametrize("mode", ["bf16", "f32", "rms", "silu"])
+@pytest.mark.parametrize("n,k", [(2048, 2048), (4096, 2048), (2048, 6144), (1000, 256), (3, 512)])
+@pytest.mark.parametrize("res", [False, True])
+def test_gemv_matches_fp32_reference(mode, n, k, res):
+    """tq_gemv against W x' in float64 over the same bf16 x' (the prologue
+    output the PyTorch ops produce); one bf16 rounding of an fp32 sum."""
+    g = torch.Generator(device="cuda").manual_seed(n + k)
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    nw = (torch.rand(k, generator=g, device="cuda") + 0.5).to(torch.bfloat16)
+    if mode == "silu":
+        x = torch.randn(2 * k, generator=g, device="cuda").to(torch.bfloat16)
+        xp = ops.silu_mul(x.reshape(1, -1)).reshape(-1)
+    elif mode == "f32":
+        x = torch.randn(k, generator=g, device="cuda")
+        xp = x.to(torch.bfloat16)
+    elif mode == "rms":
+        x = torch.randn(k, generator=g, device="cuda").to(torch.bfloat16)
+        xp = ops.rmsnorm(x.reshape(1, -1), nw, 1e-6).reshape(-1)
+    else:
+        x = torch.randn(k, generator=g, device="cuda").to(torch.bfloat16)
+        xp = x
+    r = torch.randn(n, generator=g, device="cuda").to(torch.bfloat16) if res else None
+    got = ops.gemv(w, x, mode=mode, norm_weight=nw, eps=1e-6, residual=r).double()
+    want = w.double() @ xp.double() + (r.double() if res else 0)
+    tol = 2.0 ** -7 * want.abs() + 1e-3
+    assert bool(((got - want).abs() <= tol).all()), float((got - want).abs().max())

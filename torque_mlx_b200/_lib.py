@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple] = {
     "tq_rope_qk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
                            c_void_p]),
     "tq_silu_mul": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "tq_gemv": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_float, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "tq_lse_merge": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p,
                              c_void_p, c_void_p]),
 }

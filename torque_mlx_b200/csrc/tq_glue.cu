@@ -103,6 +103,162 @@ silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int f, int64_t rows, __nv_
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// GEMV for one token: y[n] = bf16(sum_k W[n, k] x[k] (+ residual[n])), W the
+// [N, K] bf16 weight of a linear layer (PyTorch layout), fp32 accumulation.
+// The input vector is built once per CTA in shared memory (as the bf16
+// values the separate PyTorch ops would produce) by one of four prologues:
+//   kGemvBf16   x as given (bf16)
+//   kGemvF32    bf16(x) of an fp32 vector (the attention output)
+//   kGemvRms    rmsnorm(x, norm_w, eps) of a bf16 vector
+//   kGemvSilu   bf16(bf16(silu(g)) * u) of a [g | u] bf16 row (K = f)
+// The weight stream is the whole cost: a group of wpr warps takes two rows
+// at a time, each warp a contiguous slice of k with 16-byte loads (8 weights
+// a lane, four chunks of both rows issued before the math).  wpr (1..8)
+// grows for short outputs so that every SM streams.
+// ---------------------------------------------------------------------------
+enum GemvInput { kGemvBf16 = 0, kGemvF32 = 1, kGemvRms = 2, kGemvSilu = 3 };
+constexpr int kGemvThreads = 512;
+constexpr int kGemvMaxK = 8192;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4& w, float (&f)[8]) {
+  const uint32_t r[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(r[i] << 16);
+    f[2 * i + 1] = __uint_as_float(r[i] & 0xffff0000u);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_kernel(const __nv_bfloat16* __restrict__ W, const void* __restrict__ x, const __nv_bfloat16* __restrict__ norm_w,
+            float eps, const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ y, int N, int K,
+            int wpr) {
+  extern __shared__ __align__(16) __nv_bfloat16 xs[];  // [K]
+  __shared__ float red[kGemvThreads / 32];
+  __shared__ float part_s[2 * (kGemvThreads / 32)];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chunks = K / 256;  // 16-byte chunks a lane takes per row (K multiple of 256)
+  const int groups = (kGemvThreads / 32) / wpr;
+  const int g = warp / wpr, part = warp - g * wpr;
+  const int c_lo = part * chunks / wpr, c_hi = (part + 1) * chunks / wpr;
+
+  // The weights depend on no earlier kernel: pull this warp's first row pair
+  // into L2 before waiting for the previous kernel (programmatic dependent
+  // launch) and building the input vector.
+  {
+    const int n0 = blockIdx.x * groups * 2 + 2 * g;
+    for (int r = n0; r < n0 + 2 && r < N; ++r)
+      for (int c = c_lo; c < c_hi; ++c)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(W + (int64_t)r * K + (int64_t)(c * 32 + lane) * 8));
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // ---- prologue: the input vector as bf16 in shared memory ----
+  if (MODE == kGemvRms) {
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+    float ss = 0.f;
+    for (int k = tid; k < K; k += kGemvThreads) {
+      const float v = __bfloat162float(xb[k]);
+      ss = fmaf(v, v, ss);
+    }
+    const float inv = rsqrtf(block_sum<kGemvThreads>(ss, red) / (float)K + eps);
+    for (int k = tid; k < K; k += kGemvThreads)
+      xs[k] = __float2bfloat16_rn(
+          __fmul_rn(bf16_round(__fmul_rn(__bfloat162float(xb[k]), inv)), __bfloat162float(norm_w[k])));
+  } else if (MODE == kGemvSilu) {
+    const __nv_bfloat16* gu = reinterpret_cast<const __nv_bfloat16*>(x);
+    for (int k = tid; k < K; k += kGemvThreads) {
+      const float g = __bfloat162float(gu[k]), u = __bfloat162float(gu[K + k]);
+      xs[k] = __float2bfloat16_rn(__fmul_rn(bf16_round(g / (1.f + expf(-g))), u));
+    }
+  } else if (MODE == kGemvF32) {
+    const float* xf = reinterpret_cast<const float*>(x);
+    for (int k = tid; k < K; k += kGemvThreads) xs[k] = __float2bfloat16_rn(xf[k]);
+  } else {
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(x);
+    for (int k = tid; k < K; k += kGemvThreads) xs[k] = xb[k];
+  }
+  __syncthreads();
+  // the next kernel may start its own prologue-free part (weight prefetch)
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  // ---- rows: a group of wpr warps takes two rows, each warp a slice of k ----
+  const uint4* xv = reinterpret_cast<const uint4*>(xs);
+  for (int base = blockIdx.x * groups * 2; base < N; base += gridDim.x * groups * 2) {  // uniform per CTA
+    const int n0 = base + 2 * g;
+    const bool one = n0 < N, two = n0 + 1 < N;
+    float a0 = 0.f, a1 = 0.f;
+    if (one) {
+      const uint4* w0 = reinterpret_cast<const uint4*>(W + (int64_t)n0 * K);
+      const uint4* w1 = reinterpret_cast<const uint4*>(W + (int64_t)(two ? n0 + 1 : n0) * K);
+      int c = c_lo;
+      for (; c + 4 <= c_hi; c += 4) {
+        uint4 r0[4], r1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          r0[i] = __ldcs(w0 + (c + i) * 32 + lane);
+          r1[i] = __ldcs(w1 + (c + i) * 32 + lane);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float xf[8], f0[8], f1[8];
+          bf16x8_to_f32(xv[(c + i) * 32 + lane], xf);
+          bf16x8_to_f32(r0[i], f0);
+          bf16x8_to_f32(r1[i], f1);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            a0 = fmaf(f0[j], xf[j], a0);
+            a1 = fmaf(f1[j], xf[j], a1);
+          }
+        }
+      }
+      for (; c < c_hi; ++c) {
+        const uint4 r0 = __ldcs(w0 + c * 32 + lane), r1 = __ldcs(w1 + c * 32 + lane);
+        float xf[8], f0[8], f1[8];
+        bf16x8_to_f32(xv[c * 32 + lane], xf);
+        bf16x8_to_f32(r0, f0);
+        bf16x8_to_f32(r1, f1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          a0 = fmaf(f0[j], xf[j], a0);
+          a1 = fmaf(f1[j], xf[j], a1);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      a0 += __shfl_xor_sync(FULL, a0, o);
+      a1 += __shfl_xor_sync(FULL, a1, o);
+    }
+    if (wpr > 1) {  // the group's slices meet in shared memory
+      if (lane == 0) {
+        part_s[2 * warp] = a0;
+        part_s[2 * warp + 1] = a1;
+      }
+      __syncthreads();
+      if (part == 0) {
+        a0 = a1 = 0.f;
+        for (int q = 0; q < wpr; ++q) {
+          a0 += part_s[2 * (warp + q)];
+          a1 += part_s[2 * (warp + q) + 1];
+        }
+      }
+      __syncthreads();
+    }
+    if (one && part == 0 && lane == 0) {
+      if (residual) {
+        a0 += __bfloat162float(residual[n0]);
+        if (two) a1 += __bfloat162float(residual[n0 + 1]);
+      }
+      y[n0] = __float2bfloat16_rn(a0);
+      if (two) y[n0 + 1] = __float2bfloat16_rn(a1);
+    }
+  }
+}
+
 }  // namespace tq
 
 using namespace tq;
@@ -141,6 +297,70 @@ int tq_silu_mul(const void* gate_up, int64_t rows, int f, void* y, tq_stream_t s
   if (grid > 148 * 16) grid = 148 * 16;
   silu_mul_kernel<<<(unsigned)grid, kGlueThreads, 0, (cudaStream_t)stream>>>(
       (const __nv_bfloat16*)gate_up, f, rows, (__nv_bfloat16*)y);
+  return launch_status();
+}
+
+int tq_gemv(const void* weight, const void* x, int x_mode, const void* norm_weight, float eps,
+            const void* residual, void* y, int n, int k, tq_stream_t stream) {
+  if (n <= 0 || k <= 0 || k % 256 || k > kGemvMaxK) return TQ_E_SHAPE;
+  if (x_mode < kGemvBf16 || x_mode > kGemvSilu) return TQ_E_ARG;
+  if (!weight || !x || !y || (x_mode == kGemvRms && !norm_weight)) return TQ_E_ARG;
+  if ((uintptr_t)weight % 16) return TQ_E_SHAPE;
+  // SMs and resident CTAs per SM (the same for every mode: one kernel body)
+  static int sms = 0, per_sm = 1;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_kernel<kGemvRms>, kGemvThreads,
+                                                      (size_t)kGemvMaxK * sizeof(__nv_bfloat16)) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+  }
+  const size_t smem = (size_t)k * sizeof(__nv_bfloat16);
+  // warps per row pair: the smallest power of two that fills the resident wave
+  int wpr = 1;
+  while (wpr < 8 && wpr * 2 <= k / 256 && (int64_t)n * wpr < (int64_t)per_sm * sms * 2 * (kGemvThreads / 32)) wpr *= 2;
+  const int rows_per_cta = 2 * (kGemvThreads / 32) / wpr;
+  // one resident wave: every CTA builds the input vector once and streams
+  // row groups grid-stride, the same number of rounds for every CTA (a grid
+  // of all resident slots would leave most of them idle in a last partial
+  // round)
+  const int tasks = (n + rows_per_cta - 1) / rows_per_cta;
+  const int slots = per_sm * sms;
+  const int rounds = (tasks + slots - 1) / slots;
+  const int grid = (tasks + rounds - 1) / rounds;
+  cudaStream_t st = (cudaStream_t)stream;
+  const __nv_bfloat16* w = (const __nv_bfloat16*)weight;
+  const __nv_bfloat16* nw = (const __nv_bfloat16*)norm_weight;
+  const __nv_bfloat16* res = (const __nv_bfloat16*)residual;
+  __nv_bfloat16* out = (__nv_bfloat16*)y;
+  // programmatic dependent launch: the kernel may be scheduled while the
+  // previous kernel in the stream finishes; it waits (griddepcontrol.wait)
+  // before touching anything that kernel wrote
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const void* xp = x;
+  cudaError_t e;
+  switch (x_mode) {
+    case kGemvBf16: e = cudaLaunchKernelEx(&cfg, gemv_kernel<kGemvBf16>, w, xp, nw, eps, res, out, n, k, wpr); break;
+    case kGemvF32: e = cudaLaunchKernelEx(&cfg, gemv_kernel<kGemvF32>, w, xp, nw, eps, res, out, n, k, wpr); break;
+    case kGemvRms: e = cudaLaunchKernelEx(&cfg, gemv_kernel<kGemvRms>, w, xp, nw, eps, res, out, n, k, wpr); break;
+    default: e = cudaLaunchKernelEx(&cfg, gemv_kernel<kGemvSilu>, w, xp, nw, eps, res, out, n, k, wpr); break;
+  }
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return TQ_E_CUDA;
+  }
   return launch_status();
 }
 

@@ -153,31 +153,31 @@ class PackedKVDecoder:
 
     # -- one generated token --------------------------------------------------------
     def _step_body(self, token: torch.Tensor, captured: bool) -> torch.Tensor:
-        """One token through every layer: tq_rmsnorm, the qkv GEMM, tq_rope_qk,
-        the fused packed-KV step, the output GEMM with the residual folded in
-        (addmm), tq_rmsnorm, gate/up GEMM, tq_silu_mul and the down GEMM with
-        the residual: ten launches a layer."""
+        """One token through every layer in seven launches a layer:
+        tq_gemv (RMSNorm fused) for qkv, tq_rope_qk, the fused packed-KV step
+        (decode kernel packing the token + split merge), tq_gemv for the
+        output projection with the residual, tq_gemv (RMSNorm fused) for
+        gate/up and tq_gemv (SwiGLU fused) for down with the residual."""
         cfg = self.cfg
         H, Hkv, d = cfg.q_heads, cfg.kv_heads, cfg.head_dim
         # index_select keeps the lookup on the device (graph-safe, no host sync)
-        x = torch.index_select(self.embed, 0, token.reshape(1))
+        x = torch.index_select(self.embed, 0, token.reshape(1)).reshape(-1)
         qf, kr = self._qf, self._kr
         for lay, cache in zip(self.layers, self.caches):
-            h = ops.rmsnorm(x, lay["attn_norm"], cfg.rms_eps)
-            qkv = h @ lay["wqkv"].T
+            qkv = ops.gemv(lay["wqkv"], x, mode="rms", norm_weight=lay["attn_norm"], eps=cfg.rms_eps)
             ops.rope_qk(qkv, self.cos, self.sin, self.pos, H, Hkv, d, qf, kr)
-            v = qkv[:, (H + Hkv) * d:]
+            v = qkv[(H + Hkv) * d:]
             if captured:
                 # one fused launch packs the token and attends (tq_decode_append)
                 att = cache._step(kr.reshape(1, 1, Hkv, 1, d), v.reshape(1, 1, Hkv, 1, d), qf, H,
                                   advance=True, return_lse=False, full_capacity=True)[0]
             else:
                 att = cache.append_decode(key=kr, value=v.reshape(Hkv, d), query=qf)
-            x = torch.addmm(x, att.reshape(1, H * d).to(x.dtype), lay["wo"].T)
-            h = ops.rmsnorm(x, lay["mlp_norm"], cfg.rms_eps)
-            x = torch.addmm(x, ops.silu_mul(h @ lay["w_gate_up"].T), lay["w_down"].T)
+            x = ops.gemv(lay["wo"], att.reshape(-1), mode="f32", residual=x)
+            gu = ops.gemv(lay["w_gate_up"], x, mode="rms", norm_weight=lay["mlp_norm"], eps=cfg.rms_eps)
+            x = ops.gemv(lay["w_down"], gu, mode="silu", residual=x)
         self.pos.add_(1)
-        return ops.rmsnorm(x, self.final_norm, cfg.rms_eps) @ self.lm_head.T
+        return ops.gemv(self.lm_head, x, mode="rms", norm_weight=self.final_norm, eps=cfg.rms_eps).reshape(1, -1)
 
     @torch.no_grad()
     def step(self, token: torch.Tensor) -> torch.Tensor:

@@ -338,3 +338,26 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     out = torch.empty(gate_up.shape[:-1] + (f,), dtype=torch.bfloat16, device=gate_up.device) if out is None else out
     _lib.check(lib.tq_silu_mul(gate_up.data_ptr(), rows, f, out.data_ptr(), _lib.stream_ptr()), "silu_mul")
     return out
+
+
+_GEMV_MODES = {"bf16": 0, "f32": 1, "rms": 2, "silu": 3}
+
+
+def gemv(weight: torch.Tensor, x: torch.Tensor, *, mode: str = "bf16", norm_weight: torch.Tensor | None = None,
+         eps: float = 0.0, residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One-token linear layer ``y = W x' (+ residual)`` (tq_gemv): ``weight``
+    [n, k] bf16; ``x'`` is ``x`` (mode "bf16"), bf16 of an fp32 ``x`` ("f32"),
+    its RMSNorm ("rms", with ``norm_weight`` / ``eps``) or the SwiGLU
+    activation of a [gate | up] row ("silu").  Returns bf16 [n]."""
+    lib = _lib.load()
+    _bf16_rows(weight, "weight")
+    n, k = weight.shape
+    want = 2 * k if mode == "silu" else k
+    if x.numel() != want or not x.is_contiguous() or x.dtype != (torch.float32 if mode == "f32" else torch.bfloat16):
+        raise ValueError(f"gemv: x must be a contiguous {'fp32' if mode == 'f32' else 'bf16'} vector of {want}")
+    if residual is not None and (residual.numel() != n or residual.dtype != torch.bfloat16):
+        raise ValueError("gemv: residual must be bf16 with n elements")
+    out = torch.empty(n, dtype=torch.bfloat16, device=weight.device) if out is None else out
+    _lib.check(lib.tq_gemv(weight.data_ptr(), x.data_ptr(), _GEMV_MODES[mode], _lib.ptr(norm_weight), float(eps),
+                           _lib.ptr(residual), out.data_ptr(), n, k, _lib.stream_ptr()), "gemv")
+    return out
