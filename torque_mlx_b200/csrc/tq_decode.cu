@@ -276,6 +276,9 @@ static Plan make_plan(int64_t units, int G, int D, int bits, int64_t max_len, in
   // (rounding up would leave a nearly empty second wave); many units: about
   // four waves of CTAs so the ragged tails even out
   int64_t splits = uu < wave ? wave / uu : (4 * wave + uu - 1) / uu;
+  // (a single-split plan - one tile range per unit - writes its rows from
+  // the decode kernel; fewer, longer splits were measured slower than the
+  // merge launch they save)
   const int64_t max_splits = (len + tile - 1) / tile;
   if (splits > max_splits) splits = max_splits;
   if (splits * pl.warps > kMergeMaxParts) splits = kMergeMaxParts / pl.warps;  // merge weighs parts in smem
@@ -405,6 +408,11 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   p.new_dtype = TQ_F32;
   p.rotate_new_k = p.rotate_new_v = 0;
   p.k_slab_w = p.v_slab_w = nullptr;
+  // a single-split tensor plan writes the final rows from the decode kernel
+  const bool direct = pl.mode == TQ_DECODE_TENSOR && pl.splits == 1;
+  p.out = direct ? out : nullptr;
+  p.lse = direct ? lse : nullptr;
+  p.inverse_rotate = inverse_rotate_output;
 
   cudaStream_t st = (cudaStream_t)stream;
   if (app) {
@@ -441,10 +449,11 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   int s = launch_status();
   if (s != TQ_OK) return s;
 
-  const int nparts = pl.splits * pl.warps;
-  const int64_t rows = units * group_size;
   int32_t* adv = (app && app->advance) ? app->lengths : nullptr;
   const int64_t adv_n = units / (units_per_seq > 0 ? units_per_seq : 1);
+  if (direct) return adv ? tq_lengths_add(adv, (int)adv_n, 1, stream) : TQ_OK;
+  const int nparts = pl.splits * pl.warps;
+  const int64_t rows = units * group_size;
   if (head_dim == 64) launch_merge<64>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
   else if (head_dim == 128) launch_merge<128>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
   else launch_merge<256>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);

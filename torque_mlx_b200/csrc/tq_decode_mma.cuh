@@ -33,6 +33,7 @@
 #pragma once
 
 #include "tq_common.cuh"
+#include "tq_merge.cuh"  // kLn2
 
 namespace tq {
 
@@ -67,6 +68,10 @@ struct DecodeParams {
   int rotate_new_v;
   uint32_t* k_slab_w;    // writable views of k_slab / v_slab
   uint32_t* v_slab_w;
+  // single-split plans: the CTA writes the final rows itself (no merge kernel)
+  float* out;            // [units*G, D], null: partials to `part`
+  float* lse;            // [units*G] or null
+  int inverse_rotate;
 };
 
 // Length of unit u before clamping to max_len.
@@ -282,7 +287,8 @@ struct MmaCfg {
   static constexpr size_t MAIN_BYTES = (size_t)LUT_WORDS * 4 + (size_t)GM * D * 4;
   static constexpr size_t MERGE_BYTES =
       ((size_t)NW * FRAG + 3 * NW * GM + 2 * GM) * 4;
-  static constexpr size_t SMEM_BYTES = MAIN_BYTES > MERGE_BYTES ? MAIN_BYTES : MERGE_BYTES;
+  static constexpr size_t DIRECT_BYTES = MERGE_BYTES + (size_t)GM * D * 4;  // + the normalised rows
+  static constexpr size_t SMEM_BYTES = MAIN_BYTES > DIRECT_BYTES ? MAIN_BYTES : DIRECT_BYTES;
 };
 
 // Raw code words of one 16-token tile of a lane.
@@ -630,6 +636,7 @@ decode_mma_kernel(DecodeParams p) {
     fin_l[tid] = L;
   }
   __syncthreads();
+  float* rows = fin_l + GM;  // [GM][D] normalised rows (single-split plans)
   // element i of a warp's fragment slab = (nt, mb, e, lane) -> (head, dim)
   for (int i = tid; i < C::FRAG; i += NW * 32) {
     const int ln = i & 31, e = (i >> 5) & 3, blk = i >> 7;
@@ -640,7 +647,24 @@ decode_mma_kernel(DecodeParams p) {
     float acc = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) acc = fmaf(frag[w * C::FRAG + i], scale[w * GM + g], acc);
-    p.part[((u * G + g) * (int64_t)p.splits + split) * (D + 2) + dim] = acc;
+    if (p.out) rows[g * D + dim] = fin_l[g] > 0.f ? acc / fin_l[g] : 0.f;
+    else p.part[((u * G + g) * (int64_t)p.splits + split) * (D + 2) + dim] = acc;
+  }
+  if (p.out) {
+    // one split: the unit's rows are final (normalised, optionally rotated back)
+    __syncthreads();
+    for (int g = warp; g < G; g += NW) {
+      float v[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) v[j] = rows[g * D + j * 32 + lane];
+      if (p.inverse_rotate) warp_rotate<D>(v, lane, p.signs_left, p.signs_right);
+      float* o = p.out + (u * G + g) * D;
+#pragma unroll
+      for (int j = 0; j < E; ++j) o[j * 32 + lane] = v[j];
+      if (p.lse && lane == 0)
+        p.lse[u * G + g] = (fin_l[g] > 0.f) ? (fin_m[g] + log2f(fin_l[g])) * kLn2 : -INFINITY;
+    }
+    return;
   }
   if (tid < G && tid < GM) {
     float* dst = p.part + ((u * G + tid) * (int64_t)p.splits + split) * (D + 2);
