@@ -26,15 +26,18 @@ def test_shard_batch_covers_everything():
             assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
 
 
+@pytest.mark.parametrize("last", [False, True])
 @pytest.mark.parametrize("world,prefill", [(2, 10), (3, 100), (8, 131072), (4, 2)])
-def test_sequence_plan_is_consistent(world, prefill):
-    plan = SequencePlan(world=world, prefill=prefill)
+def test_sequence_plan_is_consistent(world, prefill, last):
+    plan = SequencePlan(world=world, prefill=prefill, append_to_last=last)
     length = prefill + 23
     owners = [plan.owner(p) for p in range(length)]
     for r in range(world):
         a, b = plan.prefill_range(r)
         assert all(owners[p] == r for p in range(a, b))
         assert plan.local_count(r, length) == owners.count(r)
+    if last:  # graph-captured steps: every new token lands on the last rank
+        assert all(o == world - 1 for o in owners[prefill:])
 
 
 def _free_port() -> int:
