@@ -265,8 +265,12 @@ static Plan make_plan(int64_t units, int G, int D, int bits, int64_t max_len, in
   // for batched decode (at least two units per SM) and for a few long units
   // (at most SMs/8, each split over >= 8 SMs); in between, 8-warp CTAs (two
   // per SM) spread the units over more SMs.
+  // Short caches (< 4096 tokens) with few units stay on 8-warp CTAs: each
+  // split is then one or two tiles a warp and the wider CTA's table build and
+  // merge do not pay (measured on the 28-layer decoder's ~1K-token layers).
   const bool wide_ok = pl.mode == TQ_DECODE_TENSOR && D <= 128;
-  pl.nw = (wide_ok && (units >= 2 * (int64_t)sms || units * 8 <= (int64_t)sms)) ? kMmaWarpsWide : kMmaWarps;
+  const bool batched = units >= 2 * (int64_t)sms;
+  pl.nw = (wide_ok && (batched || (units * 8 <= (int64_t)sms && max_len >= 4096))) ? kMmaWarpsWide : kMmaWarps;
   const int tile = pl.mode == TQ_DECODE_TENSOR ? pl.nw * 16 : kExactWarps * 32;
   const int per_sm = pl.mode == TQ_DECODE_TENSOR ? mma_blocks_per_sm(D, bits, G, pl.nw) : 4;
   const int64_t wave = (int64_t)sms * per_sm;
