@@ -112,6 +112,19 @@ int tq_append_kv(const void* k, const void* v, int x_dtype, int64_t groups, int 
                  const int32_t* start_pos, int groups_per_seq, int64_t pos_offset,
                  tq_stream_t stream);
 
+/* words_a[r, :] = pack(count_k(values_a[r, i] > boundaries_a[k])) for rows r of
+ * already-rotated fp32 values [rows, head_dim], and the same for the b set
+ * when values_b != NULL: the boundary-count quantizer of the MLX path
+ * (quantize_mlx, quantization.py:139-148) fused with LSB-first packing.
+ * boundaries_* hold 2^bits - 1 fp32 midpoints (codebook_boundaries,
+ * quantization.py:128-136).  Replaces quantize_and_pack_rows_metal and
+ * quantize_and_pack_rows_dual_metal (mlx_ops.py:342-412).  A value exactly on
+ * a boundary takes the lower code, which can differ from tq_quantize's
+ * nearest-centroid rule at exact midpoints (as the reference's two rules do). */
+int tq_quantize_pack_boundaries(const float* values_a, const float* values_b, int64_t rows, int head_dim,
+                                int bits, const float* boundaries_a, const float* boundaries_b,
+                                uint32_t* words_a, uint32_t* words_b, tq_stream_t stream);
+
 /* start_pos[i] += delta for i in [0, n): advances device-resident sequence
  * lengths after an append without a host round trip. */
 int tq_lengths_add(int32_t* lengths, int n, int delta, tq_stream_t stream);
@@ -121,7 +134,10 @@ int tq_lengths_add(int32_t* lengths, int n, int delta, tq_stream_t stream);
  * ------------------------------------------------------------------------- */
 
 /* Bytes of workspace tq_decode needs for these sizes (on the current device:
- * the split plan follows its SM count and the kernel's occupancy). */
+ * the split plan follows its SM count and the kernel's occupancy).  For
+ * TQ_DECODE_AUTO the figure covers both kernels, because slabs that are not
+ * 16-byte aligned (or a unit stride that is not a multiple of 4 words) make
+ * AUTO run the exact kernel, whose plan can need more. */
 int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int bits, int64_t max_len,
                              int mode, size_t* bytes);
 
@@ -185,9 +201,14 @@ int tq_decode_append(const void* new_k, const void* new_v, int kv_dtype, int rot
  * GPU, which every GPU that loads the library holds until the process exits.
  *  - A decode whose plan needs more scratch than that (tq_decode_workspace_size
  *    reports the need) returns TQ_E_SCRATCH_LIMIT and launches nothing.
+ *  - The scratch need is that of the plan the call really runs: with
+ *    TQ_DECODE_AUTO and unaligned slabs that is the exact kernel's plan.
  *  - The first call on a device looks up that device's copy of the array
  *    (with the device current); make that first call outside any CUDA stream
- *    capture.
+ *    capture.  The address is kept per device index for the life of the
+ *    process, so the entry point serves the device's primary context only:
+ *    after cudaDeviceReset, or under a context the caller created itself, the
+ *    kept address is no longer valid.
  *  - Every call on a device shares the one array.  Calls whose kernels may run
  *    at the same time on the GPU (different streams without ordering between
  *    them) race on it and give wrong results; order them on one stream.

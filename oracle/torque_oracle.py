@@ -119,6 +119,23 @@ def quantize(x: np.ndarray, centroids: np.ndarray) -> np.ndarray:
     return out.reshape(a.shape)
 
 
+def boundaries(centroids: np.ndarray) -> np.ndarray:
+    """Midpoints of neighbouring centroids in fp32 (codebook_boundaries,
+    quantization.py:128-136)."""
+    c = np.asarray(centroids, dtype=np.float32)
+    return ((c[:-1] + c[1:]) / np.float32(2.0)).astype(np.float32)
+
+
+def quantize_boundaries(x: np.ndarray, bounds: np.ndarray) -> np.ndarray:
+    """The MLX path's quantizer: the number of boundaries each value exceeds
+    (quantize_mlx, quantization.py:139-148; the append-pack kernels of
+    mlx_ops.py:257-339 use the same count).  A value equal to a boundary
+    takes the lower code."""
+    a = np.asarray(x, dtype=np.float32)
+    b = np.asarray(bounds, dtype=np.float32)
+    return (a[..., None] > b).sum(axis=-1).astype(np.uint8)
+
+
 def pack(codes: np.ndarray, bits: int) -> np.ndarray:
     """LSB-first bitstream per vector (quantization.py:156-201): code i sits at
     bit ``i*bits``; a code that crosses a word edge spills its high bits into the

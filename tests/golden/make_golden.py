@@ -1,9 +1,10 @@
 """Generate the golden vectors that pin the oracle and the CUDA path.
 
 Run in a container where the reference (cbun/torque-mlx) source tree is
-available (default ``/root/reference``; override with ``TORQUE_REFERENCE``):
+available, naming its root with ``TORQUE_REFERENCE`` or as the first argument:
 
-    python tests/golden/make_golden.py
+    TORQUE_REFERENCE=<reference root> python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference root>
 
 The reference's numpy path imports ``mlx`` eagerly (mlx_ops.py:9 through
 __init__.py:23 and cache.py:9) but never calls it, so an empty ``mlx`` stub
@@ -23,7 +24,17 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("TORQUE_REFERENCE", "/root/reference"))
+REF: Path | None = None
+
+
+def _reference_root() -> Path:
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("TORQUE_REFERENCE")
+    if not arg:
+        raise SystemExit("usage: make_golden.py <reference root>  (or set TORQUE_REFERENCE)")
+    root = Path(arg)
+    if not (root / "src" / "torque_mlx").is_dir():
+        raise SystemExit(f"{root} does not hold src/torque_mlx")
+    return root
 
 
 def _import_reference():
@@ -45,7 +56,37 @@ def sha(a: np.ndarray) -> np.ndarray:
     return np.frombuffer(hashlib.sha256(np.ascontiguousarray(a).tobytes()).digest(), dtype=np.uint8)
 
 
+class _NumpyMx:
+    """Just enough of ``mlx.core`` on numpy to run the reference's own
+    ``quantize_mlx`` (quantization.py:139-148) unchanged: array, sum,
+    expand_dims and the two dtypes it names."""
+
+    float32 = np.float32
+    uint32 = np.uint32
+
+    @staticmethod
+    def array(x, dtype=None):
+        return np.asarray(x, dtype=dtype)
+
+    sum = staticmethod(np.sum)
+    expand_dims = staticmethod(np.expand_dims)
+
+
+def _quantize_mlx_on_numpy(Q, values, codebook):
+    core = sys.modules["mlx.core"]
+    names = ("array", "sum", "expand_dims", "float32", "uint32")
+    for n in names:
+        setattr(core, n, getattr(_NumpyMx, n))
+    try:
+        return np.asarray(Q.quantize_mlx(values, codebook))
+    finally:
+        for n in names:
+            delattr(core, n)
+
+
 def main() -> None:
+    global REF
+    REF = _reference_root()
     cache_mod, config_mod, Q, R, ROT = _import_reference()
     out: dict[str, np.ndarray] = {}
 
@@ -181,6 +222,36 @@ def main() -> None:
     art.save(art_dir, force=True)
     for k, v in w.items():
         out[f"artifact_src_{k}"] = v
+
+    # --- the MLX path's boundary-count quantizer (quantization.py:128-148), run
+    # unchanged over a numpy stand-in for mlx.core, on random rows, exact
+    # midpoints and their float neighbours
+    for b in (2, 3, 4):
+        cb = Q.build_gaussian_codebook(b, seed=0)
+        out[f"bnd_b{b}"] = Q.codebook_boundaries(cb)
+        rng = np.random.default_rng(70 + b)
+        mids = out[f"bnd_b{b}"]
+        edge = np.concatenate([mids, np.nextafter(mids, np.float32(np.inf)), np.nextafter(mids, np.float32(-np.inf))])
+        for d in (64, 128, 256):
+            x = (rng.standard_normal((12, d)) * 1.5).astype(np.float32)
+            x.reshape(-1)[: edge.size] = edge
+            out[f"qmlx_in_d{d}_b{b}"] = x
+            codes = _quantize_mlx_on_numpy(Q, x, cb)
+            out[f"qmlx_codes_d{d}_b{b}"] = codes.astype(np.uint8)
+            out[f"qmlx_words_d{d}_b{b}"] = Q.pack_indices_batched(codes.astype(np.uint8), b)
+
+    # --- TorqueArtifact.build_cache() (artifact.py:157-162) on the artifact
+    # written above, loaded back by the reference, then appended and decoded
+    loaded = A.load_torque_artifact(art_dir)
+    c = loaded.build_cache()
+    rng = np.random.default_rng(45)
+    ks = rng.standard_normal((20, 2, 2, 64)).astype(np.float32)
+    vs = rng.standard_normal((20, 2, 2, 64)).astype(np.float32)
+    for t in range(20):
+        c.append(key=ks[t], value=vs[t])
+    qa = rng.standard_normal((2, 2, 64)).astype(np.float32)
+    out["artcache_keys"], out["artcache_values"], out["artcache_query"] = ks, vs, qa
+    out["artcache_decode"] = c.decode(query=qa)
 
     np.savez_compressed(HERE / "golden.npz", **out)
     total = sum(v.nbytes for v in out.values())

@@ -132,3 +132,22 @@ def test_dual_append_primitive_and_dequantize():
     np.testing.assert_array_equal(wb, O.pack(O.quantize(bb, cb.centroids), 3))
     deq = T.dequantize_packed(wa, ca, bit_width=3, head_dim=128)
     np.testing.assert_array_equal(deq, O.dequantize(O.unpack(wa, 3, 128), ca.centroids))
+
+
+@pytest.mark.parametrize("d", [64, 128, 256])
+@pytest.mark.parametrize("b", [2, 3, 4])
+def test_boundary_pack_metal_names_bit_exact(golden, d, b):
+    """quantize_and_pack_rows[_dual]_metal keep the reference's names and
+    arguments (mlx_ops.py:342-412) and its boundary-count rule: words equal
+    the reference's quantize_mlx + pack_indices_batched, midpoints included."""
+    x = golden[f"qmlx_in_d{d}_b{b}"]
+    bnd = golden[f"bnd_b{b}"]
+    want = golden[f"qmlx_words_d{d}_b{b}"]
+    wa, wb = T.quantize_and_pack_rows_dual_metal(x, x[::-1].copy(), bnd, bnd, bit_width=b, head_dim=d)
+    np.testing.assert_array_equal(wa, want)
+    np.testing.assert_array_equal(wb, O.pack(O.quantize_boundaries(x[::-1], bnd), b))
+    np.testing.assert_array_equal(T.quantize_and_pack_rows_metal(x, bnd, bit_width=b, head_dim=d), want)
+    with pytest.raises(ValueError, match="boundaries_b must have shape"):
+        T.quantize_and_pack_rows_dual_metal(x, x, bnd, bnd[:-1], bit_width=b, head_dim=d)
+    with pytest.raises(ValueError, match="values_a and values_b must match"):
+        T.quantize_and_pack_rows_dual_metal(x, x[:3], bnd, bnd, bit_width=b, head_dim=d)

@@ -136,3 +136,15 @@ def test_lse_merge_equals_full():
     m, l2 = O.lse_merge(np.stack([p[0] for p in parts]), np.stack([p[1] for p in parts]))
     np.testing.assert_allclose(m, full, atol=1e-12)
     np.testing.assert_allclose(l2, lse, atol=1e-12)
+
+
+@pytest.mark.parametrize("b", [2, 3, 4])
+@pytest.mark.parametrize("d", [64, 128, 256])
+def test_boundary_quantizer_matches_reference_mlx_rule(golden, d, b):
+    """quantize_mlx (run by the golden script over a numpy stand-in for mlx.core)
+    against the oracle's restatement: codes and packed words bit-exact."""
+    cb = O.gaussian_codebook(b, seed=0)
+    np.testing.assert_array_equal(O.boundaries(cb), golden[f"bnd_b{b}"])
+    codes = O.quantize_boundaries(golden[f"qmlx_in_d{d}_b{b}"], golden[f"bnd_b{b}"])
+    np.testing.assert_array_equal(codes, golden[f"qmlx_codes_d{d}_b{b}"])
+    np.testing.assert_array_equal(O.pack(codes, b), golden[f"qmlx_words_d{d}_b{b}"])

@@ -79,3 +79,62 @@ def test_static_scratch_rejects_oversized_plans():
     assert status == _lib.TQ_E_SCRATCH_LIMIT
     with pytest.raises(ValueError, match="scratch"):
         _lib.check(status, "tq_decode_static")
+
+
+def test_static_scratch_unaligned_auto_takes_exact_plan():
+    """Slabs that are not 16-byte aligned make AUTO run the exact kernel.  The
+    scratch check sizes that plan, so an oversized one is refused with
+    TQ_E_SCRATCH_LIMIT (not a workspace error), and the workspace size that AUTO
+    reports covers it."""
+    lib = _lib.load()
+    units, G, d, b, n = 64, 16, 256, 4, 1 << 20
+    sizes = {}
+    for mode in (0, 1, 2):  # auto, exact, tensor
+        need = ctypes.c_size_t()
+        _lib.check(lib.tq_decode_workspace_size(units, G, d, b, n, mode, ctypes.byref(need)), "size")
+        sizes[mode] = need.value
+    assert sizes[2] <= 16 << 20 < sizes[1]
+    assert sizes[0] >= max(sizes[1], sizes[2])
+    dummy = torch.zeros(64, device="cuda")
+    odd = dummy.data_ptr() + 4  # 4-byte aligned, not 16
+    status = lib.tq_decode_static(dummy.data_ptr(), 0, None, None, odd, odd, n * (d * b // 32), None, 1, n, n,
+                                  units, G, d, b, dummy.data_ptr(), dummy.data_ptr(), ctypes.c_float(1.0),
+                                  dummy.data_ptr(), None, 0, 0, _lib.stream_ptr())
+    assert status == _lib.TQ_E_SCRATCH_LIMIT
+
+
+def test_static_scratch_unaligned_slabs_match_workspace_decode():
+    """An AUTO decode over slabs shifted off 16-byte alignment (exact kernel)
+    gives the same result through the scratch as through a workspace."""
+    lib = _lib.load()
+    rng = np.random.default_rng(8)
+    cfg = T.TorqueConfig(bit_width=4, head_dim=64, num_layers=1, kv_heads=2)
+    cache = T.TorqueKVCache(config=cfg, decode_mode="auto")
+    cache.append(key=rng.standard_normal((1, 2, 700, 64)).astype(np.float16),
+                 value=rng.standard_normal((1, 2, 700, 64)).astype(np.float16))
+    dev = torch.device("cuda")
+    kbuf = torch.zeros(cache.key_slab.numel() + 1, dtype=torch.int32, device=dev)
+    vbuf = torch.zeros_like(kbuf)
+    kbuf[1:].copy_(cache.key_slab.reshape(-1))
+    vbuf[1:].copy_(cache.value_slab.reshape(-1))
+    W = T.packed_words_for_head_dim(64, 4)
+    sl, sr = cache.rotation.device_signs()
+    ws = torch.empty(ops.workspace_bytes(2, 4, 64, 4, cache.sequence_length, "auto"), dtype=torch.uint8, device=dev)
+    for call in range(2):
+        q = torch.from_numpy(rng.standard_normal((8, 64)).astype(np.float32)).to(dev)
+        outs = []
+        for fn, extra in ((lib.tq_decode, [ws.data_ptr(), ws.numel()]), (lib.tq_decode_static, [])):
+            out = torch.full_like(q, float("nan"))
+            args = [q.data_ptr(), 1, sl.data_ptr(), sr.data_ptr(), kbuf[1:].data_ptr(), vbuf[1:].data_ptr(),
+                    cache.capacity * W, cache.device_lengths.data_ptr(), 2, 0, cache.sequence_length, 2, 4, 64, 4,
+                    cache._ck.data_ptr(), cache._cv.data_ptr(), ctypes.c_float(1 / 8), out.data_ptr(), None, 1, 0,
+                    *extra, _lib.stream_ptr()]
+            _lib.check(fn(*args), "decode")
+            outs.append(out)
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(outs[1].cpu().numpy(), outs[0].cpu().numpy(), atol=2e-5, rtol=1e-4,
+                                   err_msg=f"call {call}")
+        cache.decode_mode = "exact"  # the kernel AUTO took for the shifted slabs
+        ref = cache.decode(query=q)
+        cache.decode_mode = "auto"
+        np.testing.assert_allclose(outs[0].cpu().numpy(), ref.cpu().numpy(), atol=2e-5, rtol=1e-4)

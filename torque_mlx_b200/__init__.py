@@ -37,6 +37,8 @@ from .ops import (
     lse_merge,
     quantize_and_pack_rows,
     quantize_and_pack_rows_dual,
+    quantize_and_pack_rows_dual_metal,
+    quantize_and_pack_rows_metal,
 )
 
 __all__ = [
@@ -47,6 +49,7 @@ __all__ = [
     "decode_packed_attention_split_batched", "decode_packed_attention_split_batched_with_current", "dequantize",
     "dequantize_packed", "kv_bytes_per_token", "load_codebook", "lse_merge", "pack_indices", "pack_indices_batched",
     "packed_words_for_head_dim", "quantize", "quantize_and_pack_rows", "quantize_and_pack_rows_dual",
+    "quantize_and_pack_rows_dual_metal", "quantize_and_pack_rows_metal",
     "save_codebook", "unpack_indices", "validate_head_dim",
 ]
 from .artifact import (  # noqa: E402

@@ -45,6 +45,8 @@ SIGNATURES: dict[str, tuple] = {
     "tq_append_kv": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_int, c_int, c_void_p, c_void_p,
                              c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                              c_int, c_int64, c_void_p]),
+    "tq_quantize_pack_boundaries": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                            c_void_p, c_void_p, c_void_p]),
     "tq_lengths_add": (c_int, [c_void_p, c_int, c_int, c_void_p]),
     "tq_decode_workspace_size": (c_int, [c_int64, c_int, c_int, c_int, c_int64, c_int, POINTER(c_size_t)]),
     "tq_decode": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,

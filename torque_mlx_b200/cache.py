@@ -463,9 +463,101 @@ class TorqueKVCache:
         return mask
 
 
-# MLX-named alias for drop-in use of the grouped-query cache surface.
-TorqueKVCacheMLX = TorqueKVCache
 TorqueKVCacheB200 = TorqueKVCache
+
+DecodeStrategy = str
+SUPPORTED_DECODE_STRATEGIES: tuple[str, ...] = ("auto", "split_batched", "fused_per_head")
+
+
+@dataclass(eq=False)
+class TorqueKVCacheMLX(TorqueKVCache):
+    """Drop-in for the reference's device cache ``TorqueKVCacheMLX``
+    (cache_mlx.py:40-125): same constructor knobs and the ``decode_mlx`` /
+    ``decode_mlx_with_current`` calls with ``return_numpy``.
+
+    * ``decode_tail_capacity`` (cache_mlx.py:50): the reference keeps up to that
+      many single-token appends as dequantized fp16 rows before packing them.
+      Here every append is packed at once by the append kernel, which the
+      decode reads directly, so no tail is needed; the value is validated and
+      kept.  Results equal those of the reference's packed path (the tail
+      rows hold the same centroids, rounded to fp16).
+    * ``decode_strategy`` (cache_mlx.py:51): validated against the reference's
+      choices and reported by ``resolve_decode_strategy``; the B200 decode is
+      one fused kernel for every strategy.
+    * ``profile_decode_components`` (cache_mlx.py:52): when set,
+      ``last_decode_profile`` gets the wall time of each decode call
+      (``packed_decode_seconds``, synchronised).
+    """
+
+    decode_tail_capacity: int = 16
+    decode_strategy: DecodeStrategy = "split_batched"
+    profile_decode_components: bool = False
+
+    def __post_init__(self) -> None:
+        if self.decode_tail_capacity < 0:
+            raise ValueError("decode_tail_capacity must be non-negative")
+        if self.decode_strategy not in SUPPORTED_DECODE_STRATEGIES:
+            raise ValueError("decode_strategy must be one of " + ", ".join(SUPPORTED_DECODE_STRATEGIES))
+        super().__post_init__()
+        self.last_decode_profile: dict[str, float] = {}
+
+    def resolve_decode_strategy(self, *, sequence_length: int | None = None) -> str:
+        """cache_mlx.py:742-745: ``auto`` resolves to ``split_batched``."""
+        return self.decode_strategy if self.decode_strategy != "auto" else "split_batched"
+
+    @property
+    def _key_codes(self) -> torch.Tensor:
+        """Packed K words ``[layers, kv_heads, capacity, W]`` (int32 storage of
+        the uint32 words), as the reference's attribute of that name."""
+        return self._k[0] if self.batch_size == 1 else self._k
+
+    @property
+    def _value_codes(self) -> torch.Tensor:
+        return self._v[0] if self.batch_size == 1 else self._v
+
+    def _finalize(self, out: torch.Tensor, query_heads: int, return_numpy: bool):
+        """cache_mlx.py:340-351: numpy with the 1-layer / 1-head squeezes, or
+        the device array ``[layers, Hq, d]``."""
+        L, d = self.config.num_layers, self.config.head_dim
+        out = out.reshape(L, query_heads, d) if self.batch_size == 1 else out.reshape(-1, L, query_heads, d)
+        if not return_numpy:
+            return out
+        arr = out.cpu().numpy()
+        if self.batch_size == 1 and L == 1 and query_heads == 1:
+            return arr[0, 0]
+        if self.batch_size == 1 and L == 1:
+            return arr[0]
+        return arr
+
+    def _timed(self, fn):
+        if not self.profile_decode_components:
+            return fn()
+        import time
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = fn()
+        torch.cuda.synchronize()
+        self.last_decode_profile["packed_decode_seconds"] = time.perf_counter() - t0
+        return res
+
+    def decode_mlx(self, *, query, return_numpy: bool = True):
+        """cache_mlx.py:173-234."""
+        self.last_decode_profile = {}
+        q, hq, _ = self._norm_query(query)
+        out, _ = self._timed(lambda: self._decode(q, hq, extra=0, return_lse=False))
+        return self._finalize(out, hq, return_numpy)
+
+    def decode_mlx_with_current(self, *, query, key, value, return_numpy: bool = True):
+        """cache_mlx.py:236-302: attend the cache plus one current token that is
+        not appended."""
+        self.last_decode_profile = {}
+        q, hq, _ = self._norm_query(query)
+        k = self._norm_kv(key, "key")
+        v = self._norm_kv(value, "value")
+        if k.shape[3] != 1 or v.shape[3] != 1:
+            raise ValueError("decode_mlx_with_current expects a single current token for key/value")
+        out, _ = self._timed(lambda: self._step(k, v, q, hq, advance=False, return_lse=False))
+        return self._finalize(out, hq, return_numpy)
 
 
 class CapturedDecodeStep:

@@ -59,6 +59,49 @@ append_pack_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t gro
   warp_pack_row<D, BITS>(val, lane, c, slab + g * group_stride + pos * W);
 }
 
+// Boundary-count quantize + pack of already-rotated fp32 rows, one row per
+// warp: code = number of boundaries b[k] with x > b[k] (the MLX path's rule,
+// quantization.py:139-148 and the append-pack kernels of mlx_ops.py:257-339),
+// then the same LSB-first packing as the cache.  blockIdx.y selects the
+// (values, boundaries, words) set: 0 = a, 1 = b.
+template <int D, int BITS>
+__global__ void __launch_bounds__(kAppendWarps * 32)
+boundary_pack_kernel(const float* __restrict__ xa, const float* __restrict__ xb, int64_t rows,
+                     const float* __restrict__ ba, const float* __restrict__ bb, uint32_t* __restrict__ wa,
+                     uint32_t* __restrict__ wb) {
+  constexpr int E = D / 32;
+  constexpr int W = D * BITS / 32;
+  constexpr int NB = (1 << BITS) - 1;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kAppendWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bool second = blockIdx.y == 1;
+  const float* x = (second ? xb : xa) + row * D;
+  const float* bnd = second ? bb : ba;
+  float b[NB];
+#pragma unroll
+  for (int k = 0; k < NB; ++k) b[k] = __ldg(bnd + k);
+  uint32_t code[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const float v = x[j * 32 + lane];
+    uint32_t c = 0;
+#pragma unroll
+    for (int k = 0; k < NB; ++k) c += v > b[k] ? 1u : 0u;
+    code[j] = c;
+  }
+  warp_pack_codes<D, BITS>(code, lane, (second ? wb : wa) + row * W);
+}
+
+template <int D>
+static void launch_boundary_pack(int bits, const float* xa, const float* xb, int64_t rows, const float* ba,
+                                 const float* bb, uint32_t* wa, uint32_t* wb, cudaStream_t st) {
+  dim3 grid((unsigned)((rows + kAppendWarps - 1) / kAppendWarps), xb ? 2 : 1);
+  if (bits == 2) boundary_pack_kernel<D, 2><<<grid, kAppendWarps * 32, 0, st>>>(xa, xb, rows, ba, bb, wa, wb);
+  else if (bits == 3) boundary_pack_kernel<D, 3><<<grid, kAppendWarps * 32, 0, st>>>(xa, xb, rows, ba, bb, wa, wb);
+  else boundary_pack_kernel<D, 4><<<grid, kAppendWarps * 32, 0, st>>>(xa, xb, rows, ba, bb, wa, wb);
+}
+
 // rotation only (RotationSpec.apply / inverse)
 template <int D, typename T>
 __global__ void __launch_bounds__(256)
@@ -300,6 +343,23 @@ int tq_append_kv(const void* k, const void* v, int x_dtype, int64_t groups, int 
     launch_append_d<__nv_bfloat16>(head_dim, bits, k, v, groups, tokens, signs_left, signs_right, rotate, cent_k, cent_v, k_slab, v_slab, group_stride_words, capacity, start_pos, groups_per_seq, pos_offset, st);
   else
     return TQ_E_ARG;
+  return launch_status();
+}
+
+int tq_quantize_pack_boundaries(const float* values_a, const float* values_b, int64_t rows, int head_dim,
+                                int bits, const float* boundaries_a, const float* boundaries_b,
+                                uint32_t* words_a, uint32_t* words_b, tq_stream_t stream) {
+  if (!valid_bits(bits)) return TQ_E_BITS;
+  if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
+  if (rows < 0) return TQ_E_SHAPE;
+  if (rows == 0) return TQ_OK;
+  if (!values_a || !boundaries_a || !words_a) return TQ_E_ARG;
+  if (values_b && (!boundaries_b || !words_b)) return TQ_E_ARG;
+  if (rows > (int64_t)65535 * 65535 * kAppendWarps) return TQ_E_SHAPE;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (head_dim == 64) launch_boundary_pack<64>(bits, values_a, values_b, rows, boundaries_a, boundaries_b, words_a, words_b, st);
+  else if (head_dim == 128) launch_boundary_pack<128>(bits, values_a, values_b, rows, boundaries_a, boundaries_b, words_a, words_b, st);
+  else launch_boundary_pack<256>(bits, values_a, values_b, rows, boundaries_a, boundaries_b, words_a, words_b, st);
   return launch_status();
 }
 

@@ -105,31 +105,40 @@ __device__ __forceinline__ uint32_t nearest_code(float x, const float (&c)[1 << 
   return best;
 }
 
-// Quantize a warp-resident row (v[j] = x[j*32 + lane]) against the
-// codebook c and store its W = D*BITS/32 packed words (LSB-first: code i at
-// bit i*BITS) to dst.  The 32 codes of register j fill words j*BITS ..
-// j*BITS + BITS-1; lane j*BITS + q assembles word q of group j with one
-// warp OR-reduction and lanes 0..W-1 store.
+// Store the W = D*BITS/32 packed words of a warp-resident row of codes
+// (code[j] = code of element j*32 + lane) to dst, LSB-first: code i at bit
+// i*BITS.  The 32 codes of register j fill words j*BITS .. j*BITS + BITS-1;
+// lane j*BITS + q assembles word q of group j with one warp OR-reduction and
+// lanes 0..W-1 store.
 template <int D, int BITS>
-__device__ __forceinline__ void warp_pack_row(const float (&v)[D / 32], int lane, const float (&c)[1 << BITS],
-                                              uint32_t* dst) {
+__device__ __forceinline__ void warp_pack_codes(const uint32_t (&code)[D / 32], int lane, uint32_t* dst) {
   constexpr int E = D / 32;
   constexpr int W = D * BITS / 32;
   uint32_t out_word = 0;
 #pragma unroll
   for (int j = 0; j < E; ++j) {
-    const uint32_t code = nearest_code<BITS>(v[j], c);
 #pragma unroll
     for (int q = 0; q < BITS; ++q) {
       const int shift = BITS * lane - 32 * q;
       uint32_t part = 0;
-      if (shift >= 0 && shift < 32) part = code << shift;
-      else if (shift < 0 && shift > -BITS) part = code >> (-shift);
+      if (shift >= 0 && shift < 32) part = code[j] << shift;
+      else if (shift < 0 && shift > -BITS) part = code[j] >> (-shift);
       const uint32_t word = __reduce_or_sync(FULL, part);
       if (lane == j * BITS + q) out_word = word;
     }
   }
   if (lane < W) dst[lane] = out_word;
+}
+
+// Quantize a warp-resident row (v[j] = x[j*32 + lane]) against the codebook
+// c (nearest centroid) and store its packed words to dst.
+template <int D, int BITS>
+__device__ __forceinline__ void warp_pack_row(const float (&v)[D / 32], int lane, const float (&c)[1 << BITS],
+                                              uint32_t* dst) {
+  uint32_t code[D / 32];
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) code[j] = nearest_code<BITS>(v[j], c);
+  warp_pack_codes<D, BITS>(code, lane, dst);
 }
 
 // Element i of a row of the given dtype (TQ_F32 / TQ_F16 / TQ_BF16).

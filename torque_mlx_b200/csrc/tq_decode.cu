@@ -237,6 +237,12 @@ struct Plan {
   size_t bytes;   // workspace
 };
 
+// The tensor-core kernel reads 16-byte blocks of the slabs: it needs both
+// slabs 16-byte aligned and a unit stride of whole 16-byte blocks.
+static bool slabs_aligned(const void* k_slab, const void* v_slab, int64_t unit_stride_words) {
+  return ((uintptr_t)k_slab % 16 == 0) && ((uintptr_t)v_slab % 16 == 0) && (unit_stride_words % 4 == 0);
+}
+
 static int resolve_mode(int mode, int G) {
   if (mode == TQ_DECODE_AUTO) return G >= 2 ? TQ_DECODE_TENSOR : TQ_DECODE_EXACT;
   return mode;
@@ -351,7 +357,14 @@ int tq_decode_workspace_size(int64_t units, int group_size, int head_dim, int bi
   if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
   if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
   if (mode < TQ_DECODE_AUTO || mode > TQ_DECODE_TENSOR) return TQ_E_ARG;
-  *bytes = make_plan(units, group_size, head_dim, bits, max_len, mode).bytes;
+  size_t need = make_plan(units, group_size, head_dim, bits, max_len, mode).bytes;
+  // AUTO takes the exact kernel when the slabs are not 16-byte aligned (the
+  // pointers are not known here), so it reports enough for either plan.
+  if (mode == TQ_DECODE_AUTO) {
+    const size_t exact = make_plan(units, group_size, head_dim, bits, max_len, TQ_DECODE_EXACT).bytes;
+    if (exact > need) need = exact;
+  }
+  *bytes = need;
   return TQ_OK;
 }
 
@@ -377,9 +390,7 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   const int W = words_for(head_dim, bits);
   if (unit_stride_words < max_len * W) return TQ_E_SHAPE;
   // the bulk-copy engine needs 16-byte aligned rows of whole 16-byte blocks
-  const bool aligned = ((uintptr_t)k_slab % 16 == 0) && ((uintptr_t)v_slab % 16 == 0) &&
-                       (unit_stride_words % 4 == 0);
-  if (!aligned) {
+  if (!slabs_aligned(k_slab, v_slab, unit_stride_words)) {
     if (mode == TQ_DECODE_TENSOR) return TQ_E_SHAPE;
     mode = TQ_DECODE_EXACT;
   }
@@ -564,9 +575,15 @@ int tq_decode_static(const float* query, int rotate_query, const float* signs_le
                      int head_dim, int bits, const float* cent_k, const float* cent_v, float scale,
                      float* out, float* lse, int inverse_rotate_output, int mode,
                      tq_stream_t stream) {
+  // size the plan decode_core will run: unaligned slabs take the exact kernel
+  int eff = mode;
+  if (mode == TQ_DECODE_AUTO && k_slab && v_slab && !slabs_aligned(k_slab, v_slab, unit_stride_words))
+    eff = TQ_DECODE_EXACT;
   size_t need = 0;
-  int s = tq_decode_workspace_size(units, group_size, head_dim, bits, max_len, mode, &need);
+  int s = tq_decode_workspace_size(units, group_size, head_dim, bits, max_len, eff, &need);
   if (s != TQ_OK) return s;
+  if (eff == TQ_DECODE_AUTO)  // aligned: the resolved plan alone
+    need = make_plan(units, group_size, head_dim, bits, max_len, mode).bytes;
   if (need > TQ_DECODE_STATIC_SCRATCH_BYTES) return TQ_E_SCRATCH_LIMIT;
   void* scratch = nullptr;
   s = scratch_for_current_device(&scratch);

@@ -1,24 +1,42 @@
 // Instantiations and launcher of the tensor-core decode kernel.
 #include "tq_decode_mma.cuh"
 
+#include <atomic>
+
 namespace tq {
 
+constexpr int kMaxDevices = 64;
+
+static int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    dev = 0;
+  }
+  return dev < 0 || dev >= kMaxDevices ? 0 : dev;
+}
+
+// The dynamic shared-memory opt-in is state of the function on one device
+// (context), so it is made once per device that launches the kernel.
 template <int D, int BITS, int NT, int NW>
 static void* prepare() {
-  // the dynamic shared-memory opt-in, once per process (it is per-function state)
-  static const bool done = [] {
+  static std::atomic<unsigned long long> done{0};
+  const unsigned long long bit = 1ull << current_device();
+  if (!(done.load(std::memory_order_acquire) & bit)) {
     cudaFuncSetAttribute(decode_mma_kernel<D, BITS, NT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)MmaCfg<D, BITS, NT, NW>::SMEM_BYTES);
-    return true;
-  }();
-  (void)done;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+  }
   return (void*)decode_mma_kernel<D, BITS, NT, NW>;
 }
 
+// Resident CTAs per SM, queried once per device.
 template <int D, int BITS, int NT, int NW>
 static int occupancy() {
-  static int cached = 0;
-  if (cached) return cached;
+  static std::atomic<int> cached[kMaxDevices];
+  const int dev = current_device();
+  const int c = cached[dev].load(std::memory_order_relaxed);
+  if (c) return c;
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, prepare<D, BITS, NT, NW>(), NW * 32,
                                                     MmaCfg<D, BITS, NT, NW>::SMEM_BYTES) != cudaSuccess ||
@@ -26,7 +44,7 @@ static int occupancy() {
     cudaGetLastError();
     return mma_min_blocks<D, NW>();
   }
-  cached = blocks;
+  cached[dev].store(blocks, std::memory_order_relaxed);
   return blocks;
 }
 

@@ -278,6 +278,58 @@ def quantize_and_pack_rows_dual(values_a, values_b, codebook_a, codebook_b, *, b
     return ra, rb
 
 
+def _boundaries(b, bit_width: int, label: str) -> torch.Tensor:
+    t = _tensors.to_cuda(b, torch.float32)
+    expected = (1 << bit_width) - 1
+    if t.dim() != 1 or t.shape[0] != expected:
+        raise ValueError(f"{label} must have shape ({expected},), got {tuple(t.shape)}")
+    return t
+
+
+def quantize_and_pack_rows_dual_metal(values_a, values_b, boundaries_a, boundaries_b, *, bit_width: int,
+                                      head_dim: int):
+    """Drop-in for ``quantize_and_pack_rows_dual_metal`` (mlx_ops.py:374-412):
+    already-rotated rows ``[R, d]`` of two sets, each quantized by counting
+    the boundaries it exceeds (the MLX rule, quantization.py:139-148) and
+    packed, in one launch (tq_quantize_pack_boundaries).  Same argument
+    checks and messages as the reference."""
+    lib = _lib.load()
+    np_out = _tensors.is_numpy(values_a)
+    a = _tensors.to_cuda(values_a, torch.float32)
+    if a.dim() != 2 or a.shape[1] != head_dim:
+        raise ValueError(f"values_a must have shape (rows, {head_dim}), got {tuple(a.shape)}")
+    b = _tensors.to_cuda(values_b, torch.float32)
+    if tuple(b.shape) != tuple(a.shape):
+        raise ValueError(f"values_a and values_b must match, got {tuple(a.shape)} and {tuple(b.shape)}")
+    ba = _boundaries(boundaries_a, bit_width, "boundaries_a")
+    bb = _boundaries(boundaries_b, bit_width, "boundaries_b")
+    W = packed_words_for_head_dim(head_dim, bit_width)
+    R = int(a.shape[0])
+    wa = torch.empty((R, W), dtype=torch.int32, device=a.device)
+    wb = torch.empty((R, W), dtype=torch.int32, device=a.device)
+    _lib.check(lib.tq_quantize_pack_boundaries(a.data_ptr(), b.data_ptr(), R, head_dim, bit_width, ba.data_ptr(),
+                                               bb.data_ptr(), wa.data_ptr(), wb.data_ptr(), _lib.stream_ptr()),
+               "quantize and pack")
+    return _tensors.words_out(wa, np_out), _tensors.words_out(wb, np_out)
+
+
+def quantize_and_pack_rows_metal(values, boundaries, *, bit_width: int, head_dim: int):
+    """Drop-in for ``quantize_and_pack_rows_metal`` (mlx_ops.py:342-371): one
+    set of already-rotated rows, boundary-count quantizer, packed words."""
+    lib = _lib.load()
+    np_out = _tensors.is_numpy(values)
+    a = _tensors.to_cuda(values, torch.float32)
+    if a.dim() != 2 or a.shape[1] != head_dim:
+        raise ValueError(f"values must have shape (rows, {head_dim}), got {tuple(a.shape)}")
+    bd = _boundaries(boundaries, bit_width, "boundaries")
+    W = packed_words_for_head_dim(head_dim, bit_width)
+    R = int(a.shape[0])
+    wa = torch.empty((R, W), dtype=torch.int32, device=a.device)
+    _lib.check(lib.tq_quantize_pack_boundaries(a.data_ptr(), None, R, head_dim, bit_width, bd.data_ptr(), None,
+                                               wa.data_ptr(), None, _lib.stream_ptr()), "quantize and pack")
+    return _tensors.words_out(wa, np_out)
+
+
 def dequantize_packed(words, codebook, *, bit_width: int, head_dim: int):
     """centroids[unpack(words)] for rows of packed words -> fp32 ``[..., d]``."""
     lib = _lib.load()
