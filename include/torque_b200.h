@@ -235,6 +235,58 @@ int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, 
                  const float* signs_right, tq_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Sequence-shard decode across GPUs (one process per GPU).  New in this build:
+ * the reference runs on one device only (no counterpart).
+ *
+ * Each rank holds a share of one long sequence's tokens.  Every rank owns one
+ * exchange buffer (tq_exchange_alloc, zero-filled) and maps every other
+ * rank's buffer through its CUDA IPC handle (tq_exchange_open); the handles
+ * travel over the host process group.  tq_decode_exchange then decodes the
+ * rank's tokens and, in the launch that merges its split partials, stores the
+ * rank's normalised partial and lse into every rank's buffer over NVLink,
+ * publishes them with a system-scope flag per (rank, row), waits for the
+ * other ranks' flags (each wait bounded by timeout_ns, measured with the GPU
+ * global timer) and merges the world's partials by log-sum-exp.  Two kernel
+ * launches per step, no host round trip and no library collective; a step can
+ * be captured in a CUDA graph.  A wait that gives up writes TQ_E_TIMEOUT to
+ * *status (device int32, never cleared by the library), leaves NaN rows and
+ * returns; the host reads *status between steps.
+ * ------------------------------------------------------------------------- */
+
+#define TQ_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's exchange buffer for world ranks and rows query rows. */
+int tq_exchange_buffer_bytes(int head_dim, int world, int64_t rows, size_t* bytes);
+/* cudaMalloc + zero-fill `bytes` on the current device; *ptr gets the buffer,
+ * ipc_handle (TQ_IPC_HANDLE_BYTES) its CUDA IPC handle.  Set-up only. */
+int tq_exchange_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another process's exchange buffer from its IPC handle (peer access is
+ * enabled lazily).  Set-up only. */
+int tq_exchange_open(const void* ipc_handle, void** ptr);
+/* Unmap a buffer mapped by tq_exchange_open / free one from tq_exchange_alloc. */
+int tq_exchange_close(void* ptr);
+int tq_exchange_free(void* ptr);
+
+/* One sequence-shard decode step on this rank.  Arguments as tq_decode_append
+ * (new_k == NULL: no token is appended on this rank; then new_v must be NULL
+ * and advance 0, and len_offset is tq_decode's), plus:
+ *   exchange_bufs  device array of `world` buffer pointers, [rank] = own buffer
+ *   rank, world    this rank and the rank count (world <= 16)
+ *   epoch          device int32[rows], zero at start, advanced by each step
+ *                  (the same number of steps on every rank)
+ *   timeout_ns     bound of each wait for a peer
+ *   status         device int32 that receives TQ_E_TIMEOUT on a timeout
+ * out / lse receive the merged rows over all ranks' tokens (lse natural-log). */
+int tq_decode_exchange(const void* new_k, const void* new_v, int kv_dtype, int rotate_k, int rotate_v,
+                       int advance, const float* query, int rotate_query, const float* signs_left,
+                       const float* signs_right, uint32_t* k_slab, uint32_t* v_slab, int64_t unit_stride_words,
+                       int32_t* lengths, int units_per_seq, int64_t len_offset, int64_t max_len, int64_t units,
+                       int group_size, int head_dim, int bits, const float* cent_k, const float* cent_v,
+                       float scale, float* out, float* lse, int inverse_rotate_output, int mode, void* workspace,
+                       size_t workspace_bytes, float* const* exchange_bufs, int rank, int world, int32_t* epoch,
+                       int64_t timeout_ns, int32_t* status, tq_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Decoder glue for the end-to-end generation step (benchmark config 5, a 28-layer GQA decoder).  No
  * counterpart in the reference's C surface: these replace the PyTorch
  * elementwise ops around the KV step of the example decoder (the reference

@@ -1,6 +1,12 @@
-"""Sequence-sharded decode on the GPU path (NCCL process group; one rank per
-visible GPU up to 2, each rank a child process).  With one GPU the group has
-one rank and the test still runs the exchange and tq_lse_merge."""
+"""Sequence-sharded decode on the GPU path, one rank per visible GPU (up to 4),
+each rank a child process with an NCCL process group (used for set-up and,
+with exchange="nccl", for the all-gather).  With one GPU the group has one
+rank and the test still runs the exchange kernels.
+
+Checked against the float64 oracle over the packed words of a single cache
+that holds every token (the shards' words are the same words: the append is
+bit-exact), after eager round-robin steps and after captured steps that append
+on the last rank.  NVLS is off, as for every multi-rank test here."""
 
 from __future__ import annotations
 
@@ -21,7 +27,17 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _oracle(full, qry):
+    from oracle import torque_oracle as O
+    cfg = full.config
+    kw, vw = full.packed_words()
+    sl, sr = O.rotation_signs(cfg.head_dim, cfg.rotation_seed)
+    o, _ = O.gqa_decode(O.rotate(qry, sl, sr)[None], kw[0][None], vw[0][None], full.key_codebook.centroids,
+                        full.value_codebook.centroids, cfg.bit_width)
+    return O.rotate_inverse(o[0].astype(np.float32), sl, sr)
+
+
+def _worker(rank, world, port, exchange, q):
     import torch.distributed as dist
 
     import torque_mlx_b200 as T
@@ -40,46 +56,56 @@ def _worker(rank, world, port, q):
         plan = SequencePlan(world=world, prefill=n)
         a, b = plan.prefill_range(rank)
         cfg = T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H, fused_weights=True)
-        dec = SequenceShardedDecoder(T.TorqueKVCache(config=cfg), plan)
+        dec = SequenceShardedDecoder(T.TorqueKVCache(config=cfg), plan, exchange=exchange)
         dec.prefill(keys[:, a:b], vals[:, a:b])
-        for t in range(n, n + extra):
-            dec.append(keys[:, t], vals[:, t])
-        got = dec.decode(torch.from_numpy(qry).cuda()).cpu().numpy()
+        errs = []
         full = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H))
-        full.append(key=keys, value=vals)
-        ref = full.decode(query=qry)
-        err = float(np.max(np.abs(got - ref)))
+        full.append(key=keys[:, :n], value=vals[:, :n])
+        for t in range(n, n + extra):  # eager steps, new tokens round robin
+            got = dec.step(keys[:, t], vals[:, t], torch.from_numpy(qry).cuda()).cpu().numpy()
+            full.append(key=keys[:, t], value=vals[:, t])
+            errs.append(float(np.max(np.abs(got - _oracle(full, qry)))))
+        got = dec.decode(torch.from_numpy(qry).cuda()).cpu().numpy()
+        errs.append(float(np.max(np.abs(got - _oracle(full, qry)))))
+        if exchange == "peer":
+            dec._x.check()
+        dec.close()
         # graph-captured steps with new tokens on the last rank
         plan2 = SequencePlan(world=world, prefill=n, append_to_last=True)
-        dec2 = SequenceShardedDecoder(T.TorqueKVCache(config=cfg), plan2)
+        dec2 = SequenceShardedDecoder(T.TorqueKVCache(config=cfg), plan2, exchange=exchange)
         dec2.prefill(keys[:, a:b], vals[:, a:b])
         kt = torch.from_numpy(keys[:, n]).cuda()
         vt = torch.from_numpy(vals[:, n]).cuda()
         dec2.capture_step(kt, vt, torch.from_numpy(qry).cuda())
-        got2 = dec2.step_graph().cpu().numpy()
         full2 = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=d, kv_heads=H))
-        full2.append(key=keys[:, :n + 1], value=vals[:, :n + 1])
-        err = max(err, float(np.max(np.abs(got2 - full2.decode(query=qry)))))
-        dec2.release()
+        full2.append(key=keys[:, :n], value=vals[:, :n])
+        for _ in range(3):  # the captured token is appended again each step
+            got2 = dec2.step_graph().cpu().numpy()
+            full2.append(key=keys[:, n], value=vals[:, n])
+            errs.append(float(np.max(np.abs(got2 - _oracle(full2, qry)))))
+        if exchange == "peer":
+            dec2._x.check()
+        dec2.close()
         torch.cuda.synchronize()
-        q.put((rank, err))
+        q.put((rank, max(errs)))
     finally:
         dist.destroy_process_group()
 
 
-def test_sequence_sharded_decode_matches_single_rank():
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+def test_sequence_sharded_decode_matches_oracle(exchange):
     import torch.multiprocessing as mp
 
-    world = min(2, torch.cuda.device_count())
+    world = min(4, torch.cuda.device_count())
     ctx = mp.get_context("spawn")
     qu = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, qu)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, exchange, qu)) for r in range(world)]
     for p in procs:
         p.start()
     try:
         for p in procs:
-            p.join(timeout=180)
+            p.join(timeout=240)
             assert p.exitcode == 0
     finally:
         for p in procs:
@@ -87,4 +113,5 @@ def test_sequence_sharded_decode_matches_single_rank():
                 p.kill()
                 p.join(timeout=10)
     errs = dict(qu.get(timeout=5) for _ in range(world))
-    assert max(errs.values()) < 2e-4, errs
+    # tensor-mode decode (fp16 operands) against the float64 oracle
+    assert max(errs.values()) < 4e-3, errs

@@ -59,6 +59,16 @@ SIGNATURES: dict[str, tuple] = {
     "tq_decode_static": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
                                  c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
                                  c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "tq_exchange_buffer_bytes": (c_int, [c_int, c_int, c_int64, POINTER(c_size_t)]),
+    "tq_exchange_alloc": (c_int, [c_size_t, POINTER(c_void_p), c_void_p]),
+    "tq_exchange_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "tq_exchange_close": (c_int, [c_void_p]),
+    "tq_exchange_free": (c_int, [c_void_p]),
+    "tq_decode_exchange": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int64, c_int64,
+                                   c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+                                   c_int, c_int, c_void_p, c_size_t, c_void_p, c_int, c_int, c_void_p, c_int64,
+                                   c_void_p, c_void_p]),
     "tq_rmsnorm": (c_int, [c_void_p, c_void_p, c_float, c_int64, c_int, c_void_p, c_void_p]),
     "tq_rope_qk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
                            c_void_p]),

@@ -17,7 +17,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libtorque_b200.so"
-SOURCES = ["tq_append.cu", "tq_decode.cu", "tq_decode_mma.cu", "tq_glue.cu"]
+SOURCES = ["tq_append.cu", "tq_decode.cu", "tq_decode_mma.cu", "tq_glue.cu", "tq_peer.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -14,6 +14,7 @@
 #include "tq_common.cuh"
 #include "tq_decode_mma.cuh"  // DecodeParams, kMma*
 #include "tq_merge.cuh"
+#include "tq_exchange.cuh"
 
 #include <math.h>
 #include <mutex>
@@ -334,6 +335,18 @@ static void launch_merge(const float* part, int nparts, int64_t rows, float* out
         part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
 }
 
+template <int D>
+static void launch_exchange(const float* part, int nparts, int64_t rows, const ExchangeParams& x, float* out,
+                            float* lse, int inv, const float* sl, const float* sr, int32_t* adv, int64_t adv_n,
+                            cudaStream_t st) {
+  if (nparts >= kMergeWideParts)
+    exchange_merge_kernel<D, kMergeWarpsWide * 32><<<(unsigned)rows, kMergeWarpsWide * 32, 0, st>>>(
+        part, nparts, rows, x, out, lse, inv, sl, sr, adv, adv_n);
+  else
+    exchange_merge_kernel<D, kMergeWarps * 32><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(
+        part, nparts, rows, x, out, lse, inv, sl, sr, adv, adv_n);
+}
+
 // The new token of a fused append-and-decode step (tq_decode_append).
 struct StepAppend {
   const void* k;
@@ -378,7 +391,8 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
                        int64_t len_offset, int64_t max_len, int64_t units, int group_size, int head_dim,
                        int bits, const float* cent_k, const float* cent_v, float scale, float* out,
                        float* lse, int inverse_rotate_output, int mode, void* workspace,
-                       size_t workspace_bytes, tq_stream_t stream, const StepAppend* app) {
+                       size_t workspace_bytes, tq_stream_t stream, const StepAppend* app,
+                       const ExchangeParams* xch = nullptr) {
   if (!valid_bits(bits)) return TQ_E_BITS;
   if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
   if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
@@ -424,7 +438,7 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   p.rotate_new_k = p.rotate_new_v = 0;
   p.k_slab_w = p.v_slab_w = nullptr;
   // a single-split tensor plan writes the final rows from the decode kernel
-  const bool direct = pl.mode == TQ_DECODE_TENSOR && pl.splits == 1;
+  const bool direct = pl.mode == TQ_DECODE_TENSOR && pl.splits == 1 && !xch;
   p.out = direct ? out : nullptr;
   p.lse = direct ? lse : nullptr;
   p.inverse_rotate = inverse_rotate_output;
@@ -469,6 +483,12 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   if (direct) return adv ? tq_lengths_add(adv, (int)adv_n, 1, stream) : TQ_OK;
   const int nparts = pl.splits * pl.warps;
   const int64_t rows = units * group_size;
+  if (xch) {
+    if (head_dim == 64) launch_exchange<64>(p.part, nparts, rows, *xch, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
+    else if (head_dim == 128) launch_exchange<128>(p.part, nparts, rows, *xch, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
+    else launch_exchange<256>(p.part, nparts, rows, *xch, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
+    return launch_status();
+  }
   if (head_dim == 64) launch_merge<64>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
   else if (head_dim == 128) launch_merge<128>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
   else launch_merge<256>(p.part, nparts, rows, out, lse, inverse_rotate_output, signs_left, signs_right, adv, adv_n, st);
@@ -506,6 +526,44 @@ int tq_decode_append(const void* new_k, const void* new_v, int kv_dtype, int rot
   return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
                      units_per_seq, 1, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale, out, lse,
                      inverse_rotate_output, mode, workspace, workspace_bytes, stream, &app);
+}
+
+int tq_exchange_buffer_bytes(int head_dim, int world, int64_t rows, size_t* bytes) {
+  if (!bytes) return TQ_E_ARG;
+  if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
+  if (world < 1 || world > kExchangeMaxWorld || rows < 0) return TQ_E_SHAPE;
+  const size_t data = (size_t)exchange_data_floats(head_dim, world, rows) * sizeof(float);
+  const size_t flags = ((size_t)world * rows * sizeof(uint32_t) + 15) / 16 * 16;
+  *bytes = data + flags;
+  return TQ_OK;
+}
+
+int tq_decode_exchange(const void* new_k, const void* new_v, int kv_dtype, int rotate_k, int rotate_v,
+                       int advance, const float* query, int rotate_query, const float* signs_left,
+                       const float* signs_right, uint32_t* k_slab, uint32_t* v_slab, int64_t unit_stride_words,
+                       int32_t* lengths, int units_per_seq, int64_t len_offset, int64_t max_len, int64_t units,
+                       int group_size, int head_dim, int bits, const float* cent_k, const float* cent_v,
+                       float scale, float* out, float* lse, int inverse_rotate_output, int mode, void* workspace,
+                       size_t workspace_bytes, float* const* exchange_bufs, int rank, int world, int32_t* epoch,
+                       int64_t timeout_ns, int32_t* status, tq_stream_t stream) {
+  if (!exchange_bufs || !epoch || !status) return TQ_E_ARG;
+  if (world < 1 || world > kExchangeMaxWorld || rank < 0 || rank >= world) return TQ_E_ARG;
+  if (timeout_ns <= 0) return TQ_E_ARG;
+  if (units > 0x7fffffff / 16) return TQ_E_SHAPE;
+  ExchangeParams x{exchange_bufs, rank, world, epoch, timeout_ns, status};
+  if (!new_k) {
+    if (new_v || advance) return TQ_E_ARG;
+    return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
+                       units_per_seq, len_offset, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale,
+                       out, lse, inverse_rotate_output, mode, workspace, workspace_bytes, stream, nullptr, &x);
+  }
+  if (!new_v || !lengths || len_offset != 1) return TQ_E_ARG;
+  if (kv_dtype != TQ_F32 && kv_dtype != TQ_F16 && kv_dtype != TQ_BF16) return TQ_E_ARG;
+  if ((rotate_k || rotate_v) && (!signs_left || !signs_right)) return TQ_E_ARG;
+  StepAppend app{new_k, new_v, kv_dtype, rotate_k, rotate_v, lengths, advance};
+  return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
+                     units_per_seq, 1, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale, out, lse,
+                     inverse_rotate_output, mode, workspace, workspace_bytes, stream, &app, &x);
 }
 
 int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, int head_dim,

@@ -121,6 +121,32 @@ def decode_append_raw(*, new_k: torch.Tensor, new_v: torch.Tensor, rotate_k: boo
     _lib.check(lib.tq_decode_append(*args), "decode_append")
 
 
+def decode_exchange_raw(*, exchange, new_k: torch.Tensor | None, new_v: torch.Tensor | None, rotate_k: bool,
+                        rotate_v: bool, advance: bool, query: torch.Tensor, k_slab: torch.Tensor,
+                        v_slab: torch.Tensor, unit_stride: int, lengths: torch.Tensor, units_per_seq: int,
+                        len_offset: int, max_len: int, units: int, group_size: int, head_dim: int, bits: int,
+                        cent_k: torch.Tensor, cent_v: torch.Tensor, out: torch.Tensor,
+                        lse: torch.Tensor | None = None, rotate_query: bool = False, inverse_rotate: bool = False,
+                        signs: tuple[torch.Tensor, torch.Tensor] | None = None, scale: float | None = None,
+                        mode: str | int = "auto", workspace: Workspace | None = None) -> None:
+    """One ``tq_decode_exchange`` call: this rank's shard decode, the peer
+    exchange of the normalised partials and the cross-rank merge (see
+    include/torque_b200.h).  ``exchange`` is a ``parallel.PeerExchange``."""
+    lib = _lib.load()
+    wsp = workspace or _default_ws
+    sl, sr = signs if signs is not None else (None, None)
+    ws = wsp.get(workspace_bytes(units, group_size, head_dim, bits, max_len, mode), out.device)
+    dtype = _lib.dtype_code(new_k.dtype) if new_k is not None else _lib.TQ_F32
+    _lib.check(lib.tq_decode_exchange(
+        _lib.ptr(new_k), _lib.ptr(new_v), dtype, int(rotate_k), int(rotate_v), int(advance), query.data_ptr(),
+        int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(), v_slab.data_ptr(), unit_stride,
+        lengths.data_ptr(), units_per_seq, len_offset, max_len, units, group_size, head_dim, bits,
+        cent_k.data_ptr(), cent_v.data_ptr(), float(1.0 / sqrt(head_dim) if scale is None else scale),
+        out.data_ptr(), _lib.ptr(lse), int(inverse_rotate), decode_mode_code(mode), ws.data_ptr(), ws.numel(),
+        exchange.bufs.data_ptr(), exchange.rank, exchange.world, exchange.epoch.data_ptr(), exchange.timeout_ns,
+        exchange.status.data_ptr(), _lib.stream_ptr()), "decode_exchange")
+
+
 def _cent(c) -> torch.Tensor:
     if isinstance(c, Codebook):
         c = c.centroids

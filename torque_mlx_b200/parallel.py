@@ -87,6 +87,78 @@ def gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None) -> tuple[t
     return recv[..., :d], recv[..., d].contiguous()
 
 
+class PeerExchange:
+    """The exchange buffers of a sequence-shard group (tq_exchange_* in
+    include/torque_b200.h): this rank's zero-filled buffer plus CUDA IPC
+    mappings of every other rank's, whose handles travel over the process
+    group.  ``rows`` query rows of ``head_dim`` per step.  Set-up only: the
+    step itself (``ops.decode_exchange_raw``) needs no host involvement.
+
+    ``timeout_s`` bounds every device-side wait for a peer; a wait that gives
+    up sets ``status`` (checked by :meth:`check`)."""
+
+    def __init__(self, head_dim: int, rows: int, group=None, timeout_s: float = 1.0):
+        from . import _lib
+        self._lib = lib = _lib.load()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        on = dist.is_initialized()
+        self.rank = dist.get_rank(group) if on else 0
+        self.world = dist.get_world_size(group) if on else 1
+        self.head_dim, self.rows = head_dim, rows
+        nbytes = _lib.c_size_t(0)
+        _lib.check(lib.tq_exchange_buffer_bytes(head_dim, self.world, rows, _lib.ctypes.byref(nbytes)), "exchange")
+        self.nbytes = int(nbytes.value)
+        own = _lib.ctypes.c_void_p()
+        handle = (_lib.ctypes.c_char * 64)()
+        _lib.check(lib.tq_exchange_alloc(self.nbytes, _lib.ctypes.byref(own), handle), "exchange alloc")
+        self._own = own.value
+        got: list = [bytes(handle)]
+        if self.world > 1:
+            got = [None] * self.world
+            dist.all_gather_object(got, bytes(handle), group=group)
+        self.handle = bytes(handle)
+        self._opened: list[int] = []
+        ptrs = []
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = _lib.ctypes.c_void_p()
+            hb = (_lib.ctypes.c_char * 64).from_buffer_copy(got[r])
+            _lib.check(lib.tq_exchange_open(hb, _lib.ctypes.byref(p)), "exchange open")
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        self.epoch = torch.zeros(rows, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.group = group
+        if self.world > 1:
+            dist.barrier(group)  # every buffer is zeroed and mapped before anyone writes
+
+    def check(self) -> None:
+        """Raise if a device wait for a peer gave up since the last check."""
+        s = int(self.status.item())
+        if s != 0:
+            self.status.zero_()
+            raise RuntimeError(f"sequence-shard exchange: a peer did not arrive within "
+                               f"{self.timeout_ns / 1e9:.3g} s (status {s})")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after a barrier, so no
+        peer still writes into it)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self._lib.tq_exchange_close(p)
+        self._opened = []
+        if self.world > 1 and dist.is_initialized():
+            dist.barrier(self.group)
+        self._lib.tq_exchange_free(self._own)
+        self._own = None
+
+
 class SequenceShardedDecoder:
     """Decode one long sequence whose packed tokens are spread over the ranks
     of ``group``.  ``cache`` is this rank's TorqueKVCache (batch 1) holding its
@@ -94,7 +166,10 @@ class SequenceShardedDecoder:
     returns rotated partials — the inverse rotation runs once, after the merge,
     when ``rotate_back`` is set."""
 
-    def __init__(self, cache, plan: SequencePlan, group=None, rotate_back: bool = True):
+    def __init__(self, cache, plan: SequencePlan, group=None, rotate_back: bool = True, exchange: str = "peer",
+                 timeout_s: float = 1.0):
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange must be 'peer' or 'nccl'")
         if not cache.config.fused_weights:
             raise ValueError("the local shard cache must use fused_weights=True (rotated partials)")
         if cache.batch_size != 1:
@@ -106,6 +181,64 @@ class SequenceShardedDecoder:
         self.world = dist.get_world_size(group)
         self.rotate_back = rotate_back
         self.length = 0  # global sequence length
+        self.exchange = exchange
+        self.timeout_s = timeout_s
+        self._x: PeerExchange | None = None
+
+    # ------------------------------------------------------------ peer path
+    def _peer(self, rows: int) -> PeerExchange:
+        if self._x is None or self._x.rows != rows:
+            if self._x is not None:
+                self._x.close()
+            self._x = PeerExchange(self.cache.config.head_dim, rows, self.group, self.timeout_s)
+        return self._x
+
+    def _peer_step(self, q: torch.Tensor, hq: int, k=None, v=None, *, full_capacity: bool, out: torch.Tensor):
+        """tq_decode_exchange: local shard decode (+ the fused append of the new
+        token when this rank owns it), peer exchange, cross-rank merge."""
+        from . import ops
+        c = self.cache
+        cfg = c.config
+        units = cfg.num_layers * cfg.kv_heads
+        x = self._peer(q.shape[0])
+        if k is not None:
+            c._ensure_capacity(c.sequence_length + 1)
+        max_len = c._cap if full_capacity else min(c._cap, c.sequence_length + (1 if k is not None else 0))
+        ops.decode_exchange_raw(
+            exchange=x, new_k=None if k is None else k.reshape(units, cfg.head_dim),
+            new_v=None if v is None else v.to(k.dtype).reshape(units, cfg.head_dim),
+            rotate_k=c.rotate_keys_on_append, rotate_v=c.rotate_values_on_append, advance=k is not None, query=q,
+            k_slab=c._k, v_slab=c._v, unit_stride=c._cap * c._W, lengths=c._len_dev, units_per_seq=units,
+            len_offset=1 if k is not None else 0, max_len=max_len, units=units, group_size=hq // cfg.kv_heads,
+            head_dim=cfg.head_dim, bits=cfg.bit_width, cent_k=c._ck, cent_v=c._cv, out=out,
+            rotate_query=c.rotate_queries_on_decode, inverse_rotate=self.rotate_back, signs=c._signs,
+            mode=c.decode_mode, workspace=c._ws)
+
+    def step(self, key, value, query):
+        """One eager generation step: the owner of the next position packs the
+        token inside its decode kernel, every rank decodes its shard, and the
+        partials meet over the peer exchange.  Returns the merged output."""
+        if self.exchange != "peer":
+            self.append(key, value)
+            return self.decode(query)
+        c = self.cache
+        q, hq, shape = c._norm_query(query)
+        own = self.plan.owner(self.length) == self.rank
+        k = c._norm_kv(key, "key") if own else None
+        v = c._norm_kv(value, "value") if own else None
+        out = torch.empty_like(q)
+        self._peer_step(q, hq, k, v, full_capacity=False, out=out)
+        if own:
+            c._len_host += 1
+        self.length += 1
+        return out.reshape(shape)
+
+    def close(self) -> None:
+        """Release the exchange buffers (collective: every rank calls it)."""
+        self.release()
+        if self._x is not None:
+            self._x.close()
+            self._x = None
 
     def prefill(self, key, value) -> None:
         """Append this rank's share ``[layers, kv_heads, T_r, d]`` of the prefill."""
@@ -129,6 +262,8 @@ class SequenceShardedDecoder:
         resources.  Inputs are copied from the example tensors."""
         if not self.plan.append_to_last:
             raise ValueError("graph capture needs SequencePlan(append_to_last=True)")
+        if self.exchange == "peer":
+            return self._capture_peer(key, value, query)
         from . import ops
         c = self.cache
         self.owner = self.rank == self.world - 1
@@ -170,6 +305,37 @@ class SequenceShardedDecoder:
         torch.cuda.current_stream().wait_stream(side)
         assert self._out.shape == (rows, d)
 
+    def _capture_peer(self, key, value, query) -> None:
+        """One CUDA graph per rank holds the whole step: tq_decode_exchange
+        (the last rank also packs the new token) — two kernel launches, with
+        the exchange and the cross-rank merge on the device."""
+        c = self.cache
+        self.owner = self.rank == self.world - 1
+        self._k = c._norm_kv(key, "key").clone()
+        self._v = c._norm_kv(value, "value").to(self._k.dtype).clone()
+        q, hq, self._qshape = c._norm_query(query)
+        self._q = q.clone()
+        self._out = torch.empty_like(self._q)
+        c._ensure_capacity(c.sequence_length + 1)
+        k = self._k if self.owner else None
+        v = self._v if self.owner else None
+        self._peer(self._q.shape[0])
+        # the workspace is sized outside capture; the capture itself launches nothing
+        from . import ops
+        cfg = c.config
+        units = cfg.num_layers * cfg.kv_heads
+        c._ws.get(ops.workspace_bytes(units, hq // cfg.kv_heads, cfg.head_dim, cfg.bit_width, c._cap,
+                                      c.decode_mode), self._q.device)
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.g_step = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.g_step, stream=side, capture_error_mode="thread_local"):
+                self._peer_step(self._q, hq, k, v, full_capacity=True, out=self._out)
+        torch.cuda.current_stream().wait_stream(side)
+        self.g_local = self.g_merge = None
+
     def _gather(self) -> None:
         if dist.get_backend(self.group) == "nccl":
             dist.all_gather_into_tensor(self._recv, self._send, group=self.group)
@@ -181,6 +347,12 @@ class SequenceShardedDecoder:
         the merged output (a static buffer, overwritten by the next step)."""
         if self.owner and self.cache.capacity - self.cache.sequence_length < 1:
             raise RuntimeError("cache capacity reached: capture again")
+        if self.exchange == "peer":
+            self.g_step.replay()
+            if self.owner:
+                self.cache._len_host += 1
+            self.length += 1
+            return self._out.reshape(self._qshape)
         self.g_local.replay()
         self._gather()
         self.g_merge.replay()
@@ -191,11 +363,18 @@ class SequenceShardedDecoder:
 
     def release(self) -> None:
         """Drop the captured graphs (call before destroying the process group)."""
-        self.g_local = self.g_merge = None
+        self.g_local = self.g_merge = self.g_step = None
 
     def decode(self, query):
         """Full-sequence decode: local partial -> all-gather -> LSE merge."""
         from . import ops
+        if self.exchange == "peer":
+            np_out = not isinstance(query, torch.Tensor)
+            q, hq, shape = self.cache._norm_query(query)
+            res = torch.empty_like(q)
+            self._peer_step(q, hq, full_capacity=False, out=res)
+            res = res.reshape(shape)
+            return res.cpu().numpy() if np_out else res
         q = query if isinstance(query, torch.Tensor) else torch.as_tensor(query)
         out, lse = self.cache.decode(query=q, return_lse=True)
         shape = out.shape
