@@ -62,3 +62,16 @@ def test_fusion_and_build_cache_match_reference(golden, tmp_path):
     cache.append(key=x, value=x)
     out = cache.decode(query=rng.standard_normal((2, 2, 64)).astype(np.float32))
     assert out.shape == (2, 2, 64) and np.isfinite(out).all()
+
+
+@pytest.mark.gpu
+def test_build_cache_decodes_like_the_reference_cache(golden):
+    """A reference-written artifact, loaded here: build_cache() (the GPU cache)
+    appends and decodes the same tokens as the reference's numpy cache built
+    from the same artifact by the reference (artifact.py:157-162, golden
+    vectors from tests/golden/make_golden.py)."""
+    cache = load_torque_artifact(REF_DIR).build_cache()
+    for t in range(golden["artcache_keys"].shape[0]):
+        cache.append(key=golden["artcache_keys"][t], value=golden["artcache_values"][t])
+    out = cache.decode(query=golden["artcache_query"])
+    np.testing.assert_allclose(out, golden["artcache_decode"], atol=1e-5, rtol=1e-5)

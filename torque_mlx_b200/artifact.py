@@ -1,12 +1,17 @@
-"""Torque artifacts: fused attention weights plus the runtime profile.
+"""Torque artifacts: a directory with ``manifest.json`` and an npz of fused
+attention weights, as written by the reference (src/torque_mlx/artifact.py).
 
-Same on-disk format as the reference (src/torque_mlx/artifact.py; contract
-docs/contracts/model-artifact.md): a directory with ``manifest.json``
-(format ``torque-mlx-artifact`` v1, runtime config, K/V codebooks, weight
-names, metadata) and ``weights.npz`` (``w_q, w_k, w_v, w_o`` already fused
-with Pi).  Artifacts written by either project load in the other, and
-``build_cache()`` returns this project's GPU cache with the artifact's exact
-codebooks and rotation (artifact.py:157-162).
+The on-disk format is the reference's, so artifacts move between the two
+implementations: manifest keys, the ``torque-mlx-artifact`` / version-1 tag,
+the runtime-config and codebook objects, and the npz member names listed in
+``weight_names``.  What this module needs from an artifact is the runtime
+configuration and the two codebooks, from which ``build_cache()`` makes the
+GPU cache (artifact.py:157-162); it also writes artifacts and folds weights so
+a model converted here reads back in the reference.
+
+The manifest is handled through one field table (``_FIELDS``): each entry
+names the JSON key, whether it is required, its default and how a value is
+decoded and encoded.  Parsing, validation and writing all walk that table.
 """
 
 from __future__ import annotations
@@ -14,7 +19,7 @@ from __future__ import annotations
 import json
 from dataclasses import dataclass, field, replace
 from pathlib import Path
-from typing import Any, Mapping
+from typing import Any, Callable, Mapping
 
 import numpy as np
 
@@ -24,27 +29,72 @@ from .conversion import FusedAttentionWeights, fuse_attention_weights
 from .quantization import Codebook, build_gaussian_codebook
 from .rotation import RotationSpec
 
-ARTIFACT_FORMAT = "torque-mlx-artifact"
-ARTIFACT_VERSION = 1
-DEFAULT_WEIGHTS_FILE = "weights.npz"
-DEFAULT_MANIFEST_FILE = "manifest.json"
-_DEFAULT_WEIGHT_NAMES = {"w_q": "w_q", "w_k": "w_k", "w_v": "w_v", "w_o": "w_o"}
+FORMAT_TAG = "torque-mlx-artifact"
+FORMAT_VERSION = 1
+MANIFEST_NAME = "manifest.json"
+WEIGHTS_NAME = "weights.npz"
+PROJECTIONS = ("w_q", "w_k", "w_v", "w_o")
 
 
-def _plain(value: Any) -> Any:
-    """JSON-serialisable copy (numpy scalars -> Python scalars)."""
-    if isinstance(value, dict):
-        return {str(k): _plain(v) for k, v in value.items()}
-    if isinstance(value, (list, tuple)):
-        return [_plain(v) for v in value]
-    if isinstance(value, np.generic):
-        return value.item()
-    return value
+def _plain(v: Any) -> Any:
+    """JSON-safe copy: numpy scalars become Python numbers, tuples lists."""
+    if isinstance(v, Mapping):
+        return {str(k): _plain(x) for k, x in v.items()}
+    if isinstance(v, (list, tuple)):
+        return [_plain(x) for x in v]
+    return v.item() if isinstance(v, np.generic) else v
 
 
-@dataclass(frozen=True, slots=True)
+# runtime_config object <-> TorqueConfig (the key set is part of the format)
+_CONFIG_KEYS: tuple[tuple[str, Callable[[Any], Any]], ...] = (
+    ("bit_width", int), ("head_dim", int), ("num_layers", int), ("kv_heads", int),
+    ("fused_weights", bool), ("rotation_mode", lambda v: RotationMode(str(v))), ("rotation_seed", int),
+)
+
+
+def _config_in(obj: Any) -> TorqueConfig:
+    if not isinstance(obj, Mapping):
+        raise ValueError("manifest runtime_config is not a JSON object")
+    absent = [k for k, _ in _CONFIG_KEYS if k not in obj]
+    if absent:
+        raise ValueError(f"manifest runtime_config lacks {', '.join(absent)}")
+    return TorqueConfig(**{k: conv(obj[k]) for k, conv in _CONFIG_KEYS})
+
+
+def _config_out(cfg: TorqueConfig) -> dict[str, Any]:
+    out = {k: getattr(cfg, k) for k, _ in _CONFIG_KEYS}
+    out["rotation_mode"] = cfg.rotation_mode.value
+    return out
+
+
+def _names_in(obj: Any) -> dict[str, str]:
+    names = {str(k): str(v) for k, v in dict(obj or {}).items()}
+    return names or {p: p for p in PROJECTIONS}
+
+
+_REQUIRED = object()
+
+# (json key, attribute, default or _REQUIRED, decode, encode); default None =
+# absent keys decode from None
+_FIELDS: tuple[tuple[str, str, Any, Callable, Callable], ...] = (
+    ("format_name", "format_name", FORMAT_TAG, str, str),
+    ("format_version", "format_version", FORMAT_VERSION, int, int),
+    ("model_name", "model_name", _REQUIRED, str, str),
+    ("architecture", "architecture", _REQUIRED, str, str),
+    ("source_format", "source_format", _REQUIRED, str, str),
+    ("runtime_config", "runtime_config", _REQUIRED, _config_in, _config_out),
+    ("weights_file", "weights_file", WEIGHTS_NAME, str, str),
+    ("weight_names", "weight_names", None, _names_in, dict),
+    ("key_codebook", "key_codebook", _REQUIRED, lambda v: Codebook.from_dict(dict(v)), lambda c: c.to_dict()),
+    ("value_codebook", "value_codebook", _REQUIRED, lambda v: Codebook.from_dict(dict(v)), lambda c: c.to_dict()),
+    ("extra_metadata", "extra_metadata", None, lambda v: _plain(dict(v or {})), _plain),
+)
+
+
+@dataclass(frozen=True)
 class TorqueArtifactManifest:
-    """Manifest fields and checks of artifact.py:40-137."""
+    """Parsed ``manifest.json``; the runtime config must use fused weights
+    (an artifact stores projections with the rotation folded in)."""
 
     model_name: str
     architecture: str
@@ -52,149 +102,127 @@ class TorqueArtifactManifest:
     runtime_config: TorqueConfig
     key_codebook: Codebook
     value_codebook: Codebook
-    weights_file: str = DEFAULT_WEIGHTS_FILE
-    format_name: str = ARTIFACT_FORMAT
-    format_version: int = ARTIFACT_VERSION
-    weight_names: dict[str, str] = field(default_factory=lambda: dict(_DEFAULT_WEIGHT_NAMES))
-    extra_metadata: dict[str, object] = field(default_factory=dict)
+    weights_file: str = WEIGHTS_NAME
+    format_name: str = FORMAT_TAG
+    format_version: int = FORMAT_VERSION
+    weight_names: dict[str, str] = field(default_factory=lambda: {p: p for p in PROJECTIONS})
+    extra_metadata: dict[str, Any] = field(default_factory=dict)
 
     def __post_init__(self) -> None:
+        if self.format_name != FORMAT_TAG:
+            raise ValueError(f"not a torque artifact: format_name {self.format_name!r}")
+        if self.format_version != FORMAT_VERSION:
+            raise ValueError(f"artifact format version {self.format_version} is not supported "
+                             f"(this build reads version {FORMAT_VERSION})")
         self.runtime_config.validate()
         if not self.runtime_config.fused_weights:
-            raise ValueError("Artifact runtime_config must enable fused_weights")
-        if self.format_name != ARTIFACT_FORMAT:
-            raise ValueError(f"Unsupported artifact format: {self.format_name}")
-        if self.format_version != ARTIFACT_VERSION:
-            raise ValueError(f"Unsupported artifact version: {self.format_version}")
+            raise ValueError("an artifact's runtime_config must have fused_weights = true")
+        for p in PROJECTIONS:
+            if p not in self.weight_names:
+                raise ValueError(f"manifest weight_names has no entry for {p}")
 
     @classmethod
-    def from_dict(cls, payload: Mapping[str, object]) -> "TorqueArtifactManifest":
-        required = ("model_name", "architecture", "source_format", "runtime_config", "key_codebook",
-                    "value_codebook")
-        missing = [k for k in required if k not in payload]
-        if missing:
-            raise ValueError(f"Missing required fields: {', '.join(missing)}")
-        rc = payload["runtime_config"]
-        if not isinstance(rc, Mapping):
-            raise ValueError("runtime_config must be an object")
-        config = TorqueConfig(bit_width=int(rc["bit_width"]), head_dim=int(rc["head_dim"]),
-                              num_layers=int(rc["num_layers"]), kv_heads=int(rc["kv_heads"]),
-                              fused_weights=bool(rc["fused_weights"]),
-                              rotation_mode=RotationMode(str(rc["rotation_mode"])),
-                              rotation_seed=int(rc["rotation_seed"]))
-        names = dict(payload.get("weight_names", {})) or dict(_DEFAULT_WEIGHT_NAMES)
-        return cls(model_name=str(payload["model_name"]), architecture=str(payload["architecture"]),
-                   source_format=str(payload["source_format"]), runtime_config=config,
-                   key_codebook=Codebook.from_dict(dict(payload["key_codebook"])),
-                   value_codebook=Codebook.from_dict(dict(payload["value_codebook"])),
-                   weights_file=str(payload.get("weights_file", DEFAULT_WEIGHTS_FILE)),
-                   format_name=str(payload.get("format_name", ARTIFACT_FORMAT)),
-                   format_version=int(payload.get("format_version", ARTIFACT_VERSION)),
-                   weight_names={str(k): str(v) for k, v in names.items()},
-                   extra_metadata={str(k): _plain(v) for k, v in dict(payload.get("extra_metadata", {})).items()})
+    def from_dict(cls, payload: Mapping[str, Any]) -> "TorqueArtifactManifest":
+        absent = [key for key, _, default, _, _ in _FIELDS if default is _REQUIRED and key not in payload]
+        if absent:
+            raise ValueError(f"manifest lacks required key(s): {', '.join(absent)}")
+        kwargs = {}
+        for key, attr, default, decode, _ in _FIELDS:
+            if key in payload:
+                kwargs[attr] = decode(payload[key])
+            elif default is None:
+                kwargs[attr] = decode(None)
+        return cls(**kwargs)
 
-    def to_dict(self) -> dict[str, object]:
-        rc = self.runtime_config
-        return {
-            "format_name": self.format_name, "format_version": self.format_version,
-            "model_name": self.model_name, "architecture": self.architecture,
-            "source_format": self.source_format, "variant_id": rc.variant_id,
-            "runtime_config": {"bit_width": rc.bit_width, "head_dim": rc.head_dim, "num_layers": rc.num_layers,
-                               "kv_heads": rc.kv_heads, "fused_weights": rc.fused_weights,
-                               "rotation_mode": rc.rotation_mode.value, "rotation_seed": rc.rotation_seed},
-            "weights_file": self.weights_file, "weight_names": dict(self.weight_names),
-            "key_codebook": self.key_codebook.to_dict(), "value_codebook": self.value_codebook.to_dict(),
-            "extra_metadata": _plain(self.extra_metadata),
-        }
+    def to_dict(self) -> dict[str, Any]:
+        out = {key: encode(getattr(self, attr)) for key, attr, _, _, encode in _FIELDS}
+        out["variant_id"] = self.runtime_config.variant_id
+        return out
 
 
-@dataclass(frozen=True, slots=True)
+@dataclass(frozen=True)
 class TorqueArtifact:
     manifest: TorqueArtifactManifest
     fused_weights: FusedAttentionWeights
 
-    @property
-    def runtime_config(self) -> TorqueConfig:
-        return self.manifest.runtime_config
-
-    @property
-    def key_codebook(self) -> Codebook:
-        return self.manifest.key_codebook
-
-    @property
-    def value_codebook(self) -> Codebook:
-        return self.manifest.value_codebook
+    runtime_config = property(lambda self: self.manifest.runtime_config)
+    key_codebook = property(lambda self: self.manifest.key_codebook)
+    value_codebook = property(lambda self: self.manifest.value_codebook)
 
     def build_cache(self, **cache_kwargs) -> TorqueKVCache:
-        """The drop-in hook: a GPU packed cache with this artifact's config and
-        codebooks (extra keyword arguments go to TorqueKVCache)."""
+        """The packed GPU cache for this artifact: its runtime config and both
+        codebooks (artifact.py:157-162).  Extra keywords (``batch_size``,
+        ``initial_capacity``, ``decode_mode``, ...) go to the cache."""
         return TorqueKVCache(config=self.runtime_config, key_codebook=self.key_codebook,
                              value_codebook=self.value_codebook, **cache_kwargs)
 
     def save(self, directory: str | Path, *, force: bool = False) -> Path:
+        """Write the manifest (sorted keys, indent 2) and the npz; a non-empty
+        directory is only replaced with ``force``."""
         target = Path(directory)
-        if target.exists() and any(target.iterdir()) and not force:
-            raise FileExistsError(
-                f"Refusing to overwrite non-empty artifact directory {target}; pass force=True to replace it")
+        if not force and target.is_dir() and next(target.iterdir(), None) is not None:
+            raise FileExistsError(f"{target} already holds files; use force=True to write the artifact there")
         target.mkdir(parents=True, exist_ok=True)
-        (target / DEFAULT_MANIFEST_FILE).write_text(json.dumps(self.manifest.to_dict(), indent=2, sort_keys=True),
-                                                    encoding="utf-8")
-        fw, names = self.fused_weights, self.manifest.weight_names
+        (target / MANIFEST_NAME).write_text(json.dumps(self.manifest.to_dict(), indent=2, sort_keys=True),
+                                            encoding="utf-8")
+        names = self.manifest.weight_names
         np.savez_compressed(target / self.manifest.weights_file,
-                            **{names["w_q"]: fw.w_q, names["w_k"]: fw.w_k, names["w_v"]: fw.w_v,
-                               names["w_o"]: fw.w_o})
+                            **{names[p]: getattr(self.fused_weights, p) for p in PROJECTIONS})
         return target
 
-    def summary(self) -> dict[str, object]:
-        rc, fw = self.runtime_config, self.fused_weights
+    def summary(self) -> dict[str, Any]:
+        m = self.manifest
+
+        def book(c: Codebook) -> dict[str, Any]:
+            return {"name": c.name, "bit_width": c.bit_width, "centroid_count": int(c.centroids.size)}
+
         return {
-            "format_name": self.manifest.format_name, "format_version": self.manifest.format_version,
-            "model_name": self.manifest.model_name, "architecture": self.manifest.architecture,
-            "source_format": self.manifest.source_format, "variant_id": rc.variant_id,
-            "weights_file": self.manifest.weights_file,
-            "runtime_config": self.manifest.to_dict()["runtime_config"],
-            "weight_shapes": {k: list(getattr(fw, k).shape) for k in ("w_q", "w_k", "w_v", "w_o")},
-            "key_codebook": {"name": self.key_codebook.name, "bit_width": self.key_codebook.bit_width,
-                             "centroid_count": int(self.key_codebook.centroids.size)},
-            "value_codebook": {"name": self.value_codebook.name, "bit_width": self.value_codebook.bit_width,
-                               "centroid_count": int(self.value_codebook.centroids.size)},
-            "extra_metadata": _plain(self.manifest.extra_metadata),
+            "format_name": m.format_name, "format_version": m.format_version, "model_name": m.model_name,
+            "architecture": m.architecture, "source_format": m.source_format,
+            "variant_id": m.runtime_config.variant_id, "weights_file": m.weights_file,
+            "runtime_config": _config_out(m.runtime_config),
+            "weight_shapes": {p: list(np.shape(getattr(self.fused_weights, p))) for p in PROJECTIONS},
+            "key_codebook": book(m.key_codebook), "value_codebook": book(m.value_codebook),
+            "extra_metadata": _plain(m.extra_metadata),
         }
 
     @classmethod
     def load(cls, directory: str | Path) -> "TorqueArtifact":
-        target = Path(directory)
-        mpath = target / DEFAULT_MANIFEST_FILE
-        if not mpath.exists():
-            raise FileNotFoundError(f"Artifact manifest not found: {mpath}")
+        root = Path(directory)
+        mpath = root / MANIFEST_NAME
+        if not mpath.is_file():
+            raise FileNotFoundError(f"no {MANIFEST_NAME} in {root}")
         manifest = TorqueArtifactManifest.from_dict(json.loads(mpath.read_text(encoding="utf-8")))
-        wpath = target / manifest.weights_file
-        if not wpath.exists():
-            raise FileNotFoundError(f"Artifact weights not found: {wpath}")
-        with np.load(wpath) as data:
-            ws = {k: np.asarray(data[manifest.weight_names[k]], dtype=np.float32) for k in ("w_q", "w_k", "w_v", "w_o")}
+        wpath = root / manifest.weights_file
+        if not wpath.is_file():
+            raise FileNotFoundError(f"weights file {wpath} named by the manifest is missing")
+        with np.load(wpath) as z:
+            w = {p: np.asarray(z[manifest.weight_names[p]], dtype=np.float32) for p in PROJECTIONS}
         return cls(manifest=manifest,
-                   fused_weights=FusedAttentionWeights(**ws, rotation_seed=manifest.runtime_config.rotation_seed))
+                   fused_weights=FusedAttentionWeights(**w, rotation_seed=manifest.runtime_config.rotation_seed))
+
+
+def load_torque_artifact(directory: str | Path) -> TorqueArtifact:
+    return TorqueArtifact.load(directory)
 
 
 def build_torque_artifact(*, model_name: str, architecture: str, source_format: str, config: TorqueConfig,
                           w_q, w_k, w_v, w_o, rotation: RotationSpec | None = None,
                           key_codebook: Codebook | None = None, value_codebook: Codebook | None = None,
-                          extra_metadata: Mapping[str, object] | None = None) -> TorqueArtifact:
-    """Fuse the weights and assemble an artifact (artifact.py:246-296): the
-    runtime config is forced to fused_weights, codebooks default to the
-    seeded Gaussian ones (K: rotation_seed, V: rotation_seed + 1)."""
-    rc = replace(config, fused_weights=True)
-    rotation = rotation or RotationSpec.from_seed(head_dim=rc.head_dim, seed=rc.rotation_seed)
-    key_codebook = key_codebook or build_gaussian_codebook(rc.bit_width, seed=rc.rotation_seed)
-    value_codebook = value_codebook or build_gaussian_codebook(rc.bit_width, seed=rc.rotation_seed + 1)
-    fused = fuse_attention_weights(w_q=w_q, w_k=w_k, w_v=w_v, w_o=w_o, rotation=rotation)
-    meta: dict[str, object] = {"input_dim": int(np.shape(w_q)[1]), "output_dim": int(np.shape(w_o)[0])}
-    if extra_metadata:
-        meta.update({str(k): _plain(v) for k, v in extra_metadata.items()})
-    manifest = TorqueArtifactManifest(model_name=model_name, architecture=architecture, source_format=source_format,
-                                      runtime_config=rc, key_codebook=key_codebook, value_codebook=value_codebook,
-                                      extra_metadata=meta)
+                          extra_metadata: Mapping[str, Any] | None = None) -> TorqueArtifact:
+    """Fold the rotation into the four projections (on the GPU, exact
+    rotation kernel) and describe them with a fused-weights runtime config.
+    Default codebooks follow the cache's seeds (K: rotation_seed, V: + 1)."""
+    cfg = replace(config, fused_weights=True)
+    rot = rotation or RotationSpec.from_seed(head_dim=cfg.head_dim, seed=cfg.rotation_seed)
+    kb = key_codebook or build_gaussian_codebook(cfg.bit_width, seed=cfg.rotation_seed)
+    vb = value_codebook or build_gaussian_codebook(cfg.bit_width, seed=cfg.rotation_seed + 1)
+    fused = fuse_attention_weights(w_q=w_q, w_k=w_k, w_v=w_v, w_o=w_o, rotation=rot)
+    meta: dict[str, Any] = {"input_dim": int(np.shape(w_q)[1]), "output_dim": int(np.shape(w_o)[0])}
+    meta.update(_plain(dict(extra_metadata or {})))
+    manifest = TorqueArtifactManifest(model_name=model_name, architecture=architecture,
+                                      source_format=source_format, runtime_config=cfg, key_codebook=kb,
+                                      value_codebook=vb, extra_metadata=meta)
     return TorqueArtifact(manifest=manifest, fused_weights=fused)
 
 
@@ -202,19 +230,17 @@ def convert_npz_checkpoint(*, input_path: str | Path, output_dir: str | Path, mo
                            architecture: str, source_format: str, bit_width: int, num_layers: int, kv_heads: int,
                            rotation_seed: int, head_dim: int | None = None, key_codebook: Codebook | None = None,
                            value_codebook: Codebook | None = None, force: bool = False) -> TorqueArtifact:
-    """NPZ (w_q, w_k, w_v, w_o) -> saved artifact (artifact.py:299-343)."""
-    with np.load(input_path) as ck:
-        if any(k not in ck for k in ("w_q", "w_k", "w_v", "w_o")):
-            raise ValueError("Expected NPZ checkpoint to contain w_q, w_k, w_v, and w_o arrays")
-        ws = {k: np.asarray(ck[k]) for k in ("w_q", "w_k", "w_v", "w_o")}
-    config = TorqueConfig(bit_width=bit_width, head_dim=int(ws["w_q"].shape[0]) if head_dim is None else head_dim,
-                          num_layers=num_layers, kv_heads=kv_heads, fused_weights=True, rotation_seed=rotation_seed)
+    """npz holding w_q / w_k / w_v / w_o -> artifact directory.  head_dim
+    defaults to w_q's output dimension."""
+    with np.load(input_path) as z:
+        absent = [p for p in PROJECTIONS if p not in z.files]
+        if absent:
+            raise ValueError(f"{input_path} lacks the projection array(s) {', '.join(absent)}")
+        w = {p: np.asarray(z[p]) for p in PROJECTIONS}
+    cfg = TorqueConfig(bit_width=bit_width, head_dim=int(w["w_q"].shape[0]) if head_dim is None else head_dim,
+                       num_layers=num_layers, kv_heads=kv_heads, fused_weights=True, rotation_seed=rotation_seed)
     art = build_torque_artifact(model_name=model_name or Path(input_path).stem, architecture=architecture,
-                                source_format=source_format, config=config, key_codebook=key_codebook,
-                                value_codebook=value_codebook, **ws)
+                                source_format=source_format, config=cfg, key_codebook=key_codebook,
+                                value_codebook=value_codebook, **w)
     art.save(output_dir, force=force)
     return art
-
-
-def load_torque_artifact(directory: str | Path) -> TorqueArtifact:
-    return TorqueArtifact.load(directory)
