@@ -24,7 +24,7 @@ static void* prepare() {
   const unsigned long long bit = 1ull << current_device();
   if (!(done.load(std::memory_order_acquire) & bit)) {
     cudaFuncSetAttribute(decode_mma_kernel<D, BITS, NT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)MmaCfg<D, BITS, NT, NW>::SMEM_BYTES);
+                         (int)RingCfg<D, BITS, NT, NW>::SMEM_BYTES);
     done.fetch_or(bit, std::memory_order_acq_rel);
   }
   return (void*)decode_mma_kernel<D, BITS, NT, NW>;
@@ -39,7 +39,7 @@ static int occupancy() {
   if (c) return c;
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, prepare<D, BITS, NT, NW>(), NW * 32,
-                                                    MmaCfg<D, BITS, NT, NW>::SMEM_BYTES) != cudaSuccess ||
+                                                    RingCfg<D, BITS, NT, NW>::SMEM_BYTES) != cudaSuccess ||
       blocks < 1) {
     cudaGetLastError();
     return mma_min_blocks<D, NW>();
@@ -52,7 +52,7 @@ template <int D, int BITS, int NT, int NW>
 static void launch_one(const DecodeParams& p, cudaStream_t st) {
   dim3 grid(p.splits, (unsigned)p.units);
   prepare<D, BITS, NT, NW>();
-  decode_mma_kernel<D, BITS, NT, NW><<<grid, NW * 32, MmaCfg<D, BITS, NT, NW>::SMEM_BYTES, st>>>(p);
+  decode_mma_kernel<D, BITS, NT, NW><<<grid, NW * 32, RingCfg<D, BITS, NT, NW>::SMEM_BYTES, st>>>(p);
 }
 
 template <int D, int BITS>

@@ -202,7 +202,13 @@ __device__ __forceinline__ T load_code(const T* p) {
 #endif
 }
 
-template <int NB, int W>
+template <bool SMEM, typename T>
+__device__ __forceinline__ T ld_run(const T* p) {
+  if constexpr (SMEM) return *p;
+  else return load_code(p);
+}
+
+template <int NB, int W, bool SMEM = false>
 __device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const uint32_t* row, int start) {
   constexpr int NW = Run<NB>::NW;
   if constexpr (Run<NB>::ALIGNED) {
@@ -210,21 +216,21 @@ __device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const ui
 #pragma unroll
     for (int i = 0; i < NW; i += VEC) {
       if constexpr (VEC == 4) {
-        const uint4 v = load_code(reinterpret_cast<const uint4*>(row + i));
+        const uint4 v = ld_run<SMEM>(reinterpret_cast<const uint4*>(row + i));
         raw[i] = v.x; raw[i + 1] = v.y; raw[i + 2] = v.z; raw[i + 3] = v.w;
       } else if constexpr (VEC == 2) {
-        const uint2 v = load_code(reinterpret_cast<const uint2*>(row + i));
+        const uint2 v = ld_run<SMEM>(reinterpret_cast<const uint2*>(row + i));
         raw[i] = v.x; raw[i + 1] = v.y;
       } else {
-        raw[i] = load_code(row + i);
+        raw[i] = ld_run<SMEM>(row + i);
       }
     }
   } else {
     const bool tail = start + NB > 32 * NW;  // the run reaches one more word
 #pragma unroll
-    for (int i = 0; i < NW; ++i) raw[i] = load_code(row + i);
+    for (int i = 0; i < NW; ++i) raw[i] = ld_run<SMEM>(row + i);
     raw[NW] = 0u;
-    if (tail) raw[NW] = load_code(row + NW);
+    if (tail) raw[NW] = ld_run<SMEM>(row + NW);
   }
 }
 
@@ -291,6 +297,66 @@ struct MmaCfg {
   static constexpr size_t SMEM_BYTES = MAIN_BYTES > DIRECT_BYTES ? MAIN_BYTES : DIRECT_BYTES;
 };
 
+// Per-warp staging ring: each warp streams its token range through STAGES
+// slots of one 16-token tile of K and V words, filled by the bulk-copy
+// engine (cp.async.bulk global -> shared, completion counted on one mbarrier
+// per slot).  Several tiles per warp are in flight while the warp computes,
+// without holding them in registers.  The ring follows the tables and the
+// query rows; the barriers follow the ring.  STAGES is the largest count
+// (at most 4) that fits the CTA's share of the SM's shared memory: all of it
+// for one CTA per SM, half for two.
+template <int D, int BITS, int NT, int NW>
+struct RingCfg {
+  using C = MmaCfg<D, BITS, NT, NW>;
+  static constexpr int TILE_WORDS = 16 * C::W;                    // one 16-token tile of one of K / V
+  static constexpr size_t STAGE_BYTES = 2 * (size_t)TILE_WORDS * 4;
+  static constexpr size_t BUDGET = (NW == 16 || D == 256) ? 225 * 1024 : 112 * 1024;
+  static constexpr size_t RING_OFF = (C::MAIN_BYTES + 127) / 128 * 128;
+  static constexpr size_t FIT = (BUDGET - RING_OFF - (size_t)NW * 4 * 8) / ((size_t)NW * STAGE_BYTES);
+  static constexpr int STAGES = FIT > 4 ? 4 : (int)FIT;
+  static_assert(FIT >= 2, "staging ring needs two slots per warp");
+  static constexpr size_t BAR_OFF = RING_OFF + (size_t)NW * STAGES * STAGE_BYTES;
+  static constexpr size_t RING_TOTAL = BAR_OFF + (size_t)NW * STAGES * 8;
+  static constexpr size_t SMEM_BYTES = RING_TOTAL > C::DIRECT_BYTES ? RING_TOTAL : C::DIRECT_BYTES;
+};
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Wait until the barrier's phase with this parity has completed; gives up
+// (false) after about a second of polling instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (it >= 64) __nanosleep(64);
+  }
+  return false;
+}
+
+// One bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned)
+// from this GPU's global memory into this CTA's shared memory, completing on
+// `bar`.  No multicast: the destination is the issuing CTA only.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // Raw code words of one 16-token tile of a lane.
 template <int D, int BITS>
 struct TileRegs {
@@ -321,6 +387,20 @@ __device__ __forceinline__ void load_tile(TileRegs<D, BITS>& t, const uint32_t* 
   load_raw<C::RUNV, W>(t.vb, vt + lp.v_row + W, lp.v_bit);
   load_raw<C::RUNV, W>(t.vc, vt + lp.v_row + 8 * W, lp.v_bit);
   load_raw<C::RUNV, W>(t.vd, vt + lp.v_row + 9 * W, lp.v_bit);
+}
+
+// The same lane runs, read from a 16-token tile staged in shared memory.
+template <int D, int BITS>
+__device__ __forceinline__ void load_tile_smem(TileRegs<D, BITS>& t, const uint32_t* kt, const uint32_t* vt,
+                                               const LanePlan& lp) {
+  using C = MmaCfg<D, BITS, 1>;
+  constexpr int W = C::W;
+  load_raw<C::RUNK, W, true>(t.k0, kt + lp.k_row, lp.k_bit);
+  load_raw<C::RUNK, W, true>(t.k1, kt + lp.k_row + 8 * W, lp.k_bit);
+  load_raw<C::RUNV, W, true>(t.va, vt + lp.v_row, lp.v_bit);
+  load_raw<C::RUNV, W, true>(t.vb, vt + lp.v_row + W, lp.v_bit);
+  load_raw<C::RUNV, W, true>(t.vc, vt + lp.v_row + 8 * W, lp.v_bit);
+  load_raw<C::RUNV, W, true>(t.vd, vt + lp.v_row + 9 * W, lp.v_bit);
 }
 
 // Tile that runs past the unit's last token: rows are clamped to `last`
@@ -468,11 +548,13 @@ decode_mma_kernel(DecodeParams p) {
   constexpr int KB = C::KB;
   constexpr int GM = C::GM;
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_fail;  // a staging copy never completed: the CTA's rows become NaN
   uint32_t* lut = reinterpret_cast<uint32_t*>(smem);      // interleaved K/V pair tables
   float* q_s = reinterpret_cast<float*>(lut + C::LUT_WORDS);  // [GM][D]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gr = lane >> 2, tq = lane & 3;
+  if (tid == 0) s_fail = 0;  // published by the table barrier below
   const int64_t u = blockIdx.y;
   const int split = blockIdx.x;
   const int G = p.G;
@@ -497,11 +579,45 @@ decode_mma_kernel(DecodeParams p) {
   lp.v_bit = (gr * C::RUNV) & 31;
   lp.k_row = gr * C::W + lp.k_word;
   lp.v_row = 2 * tq * C::W + lp.v_word;
-  auto fetch = [&](TileRegs<D, BITS>& t, int64_t tile0) {
-    const uint32_t* k = kbase + tile0 * C::W;
-    const uint32_t* v = vbase + tile0 * C::W;
-    if (tile0 + 16 <= n) load_tile<D, BITS>(t, k, v, lp);
-    else load_tile_clamped<D, BITS>(t, k, v, (int)(n - 1 - tile0), gr, tq, lp);
+  // ---- staging ring of this warp: S slots of [K tile | V tile] words ----
+  using RC = RingCfg<D, BITS, NT, NW>;
+  constexpr int S = RC::STAGES;
+  constexpr int TW = RC::TILE_WORDS;
+  uint32_t* ring = reinterpret_cast<uint32_t*>(smem + RC::RING_OFF) + (size_t)warp * S * 2 * TW;
+  const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+  const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(smem + RC::BAR_OFF) + (uint32_t)(warp * S * 8);
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < S; ++i) mbar_init(bar0 + 8 * i, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  const int64_t cap_rows = p.unit_stride / C::W;  // rows of the unit that may be read
+  const int ntiles = w1 > w0 ? (int)((w1 - w0 + 15) / 16) : 0;
+  // tile i of the warp's range -> slot i % S.  Tiles start at multiples of 16
+  // tokens, so both copies start on 16-byte boundaries; a whole tile is
+  // copied when the unit's storage holds its 16 rows (rows past the length
+  // are masked by the softmax), else the lanes copy the rows that exist.
+  auto issue = [&](int i) {
+    const int slot = i % S;
+    const int64_t t0 = w0 + 16 * (int64_t)i;
+    const uint32_t bar = bar0 + 8 * slot;
+    if (t0 + 16 <= cap_rows) {
+      if (lane == 0) {
+        mbar_expect_tx(bar, 2 * TW * 4);
+        bulk_g2s(ring_s + slot * 2 * TW * 4, kbase + t0 * C::W, TW * 4, bar);
+        bulk_g2s(ring_s + (slot * 2 + 1) * TW * 4, vbase + t0 * C::W, TW * 4, bar);
+      }
+    } else {
+      const int words = (int)min((int64_t)16, cap_rows - t0) * C::W;
+      uint32_t* kd = ring + slot * 2 * TW;
+      for (int w = lane; w < TW; w += 32) {
+        kd[w] = w < words ? __ldcg(kbase + t0 * C::W + w) : 0u;
+        kd[TW + w] = w < words ? __ldcg(vbase + t0 * C::W + w) : 0u;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar);
+    }
   };
   // fused append: the CTA whose chunk holds the new token packs it first
   if (p.new_k) {
@@ -509,11 +625,13 @@ decode_mma_kernel(DecodeParams p) {
     const int64_t pos = raw_n - 1;
     if (raw_n >= 1 && raw_n <= p.max_len && pos >= c0 && pos < c0 + p.chunk) {
       if (warp < 2) append_new_row<D, BITS>(p, u, pos, warp, lane);
-      __syncthreads();  // the new words are visible to the CTA's tile loads
+      // the new words were written through the generic proxy; the bulk copies
+      // that read them are async-proxy operations
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncthreads();
     }
   }
-  TileRegs<D, BITS> ta, tb;
-  if (w0 < w1) fetch(ta, w0);
+  for (int i = 0; i < S && i < ntiles; ++i) issue(i);  // in flight while the tables are built
 
   // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
   {
@@ -575,16 +693,27 @@ decode_mma_kernel(DecodeParams p) {
   }
   const uint32_t lane4 = (uint32_t)lane * 4u;
 
-  auto process = [&](const TileRegs<D, BITS>& t, int valid) {
-    tile_math<D, BITS, NT>(t, valid, lut, lp, lane4, gr, tq, qf, o, mref, mthr, lrow);
-  };
-  // ping-pong: the next tile's loads are issued before the current tile's math
-  for (int64_t t0 = w0; t0 < w1; t0 += 32) {
-    if (t0 + 16 < w1) fetch(tb, t0 + 16);
-    process(ta, (int)min((int64_t)16, w1 - t0));
-    if (t0 + 16 >= w1) break;
-    if (t0 + 32 < w1) fetch(ta, t0 + 32);
-    process(tb, (int)min((int64_t)16, w1 - t0 - 16));
+  // token loop: wait for slot i % S, compute, refill the slot with tile i + S
+  bool stalled = false;
+  int i = 0;
+  for (; i < ntiles; ++i) {
+    const int slot = i % S;
+    if (!mbar_wait(bar0 + 8 * slot, (uint32_t)(i / S) & 1u)) {
+      stalled = true;
+      break;
+    }
+    TileRegs<D, BITS> t;
+    load_tile_smem<D, BITS>(t, ring + slot * 2 * TW, ring + slot * 2 * TW + TW, lp);
+    tile_math<D, BITS, NT>(t, (int)min((int64_t)16, w1 - (w0 + 16 * (int64_t)i)), lut, lp, lane4, gr, tq, qf, o,
+                           mref, mthr, lrow);
+    __syncwarp();  // every lane has read the slot before it is refilled
+    if (i + S < ntiles) issue(i + S);
+  }
+  if (stalled) {
+    // a copy never completed: wait (bounded) for the ones still in flight so
+    // none lands after the CTA's shared memory is reused, and poison the rows
+    for (int j = i; j < ntiles && j < i + S; ++j) mbar_wait(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
+    s_fail = 1;
   }
 
   // ---- merge the warps of this CTA through shared memory (reusing the tables) ----
@@ -632,10 +761,11 @@ decode_mma_kernel(DecodeParams p) {
       scale[w * GM + tid] = f;
       L += red_l[w * GM + tid] * f;
     }
-    fin_m[tid] = M;
-    fin_l[tid] = L;
+    fin_m[tid] = s_fail ? 0.f : M;
+    fin_l[tid] = s_fail ? 1.f : L;
   }
   __syncthreads();
+  const float poison = s_fail ? __int_as_float(0x7fc00000) : 0.f;
   float* rows = fin_l + GM;  // [GM][D] normalised rows (single-split plans)
   // element i of a warp's fragment slab = (nt, mb, e, lane) -> (head, dim)
   for (int i = tid; i < C::FRAG; i += NW * 32) {
@@ -647,6 +777,7 @@ decode_mma_kernel(DecodeParams p) {
     float acc = 0.f;
 #pragma unroll
     for (int w = 0; w < NW; ++w) acc = fmaf(frag[w * C::FRAG + i], scale[w * GM + g], acc);
+    acc += poison;
     if (p.out) rows[g * D + dim] = fin_l[g] > 0.f ? acc / fin_l[g] : 0.f;
     else p.part[((u * G + g) * (int64_t)p.splits + split) * (D + 2) + dim] = acc;
   }

@@ -177,8 +177,9 @@ class SequenceShardedDecoder:
         self.cache = cache
         self.plan = plan
         self.group = group
-        self.rank = dist.get_rank(group)
-        self.world = dist.get_world_size(group)
+        on = dist.is_initialized()
+        self.rank = dist.get_rank(group) if on else 0
+        self.world = dist.get_world_size(group) if on else 1
         self.rotate_back = rotate_back
         self.length = 0  # global sequence length
         self.exchange = exchange
