@@ -102,7 +102,7 @@ def config_dict(name: str, wl: dict, world: int) -> dict:
 
 class ClockSampler:
     """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed
-    region, for the GPU named by its PCI bus id (nvidia-smi ignores
+    region, for the GPU named by its UUID (nvidia-smi ignores
     CUDA_VISIBLE_DEVICES, so the CUDA ordinal could name another GPU)."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -112,7 +112,7 @@ class ClockSampler:
     def __init__(self, cuda_index: int):
         try:
             import torch
-            self.gpu = torch.cuda.get_device_properties(cuda_index).pci_bus_id
+            self.gpu = f"GPU-{torch.cuda.get_device_properties(cuda_index).uuid}"
         except Exception:  # noqa: BLE001 - fall back to the ordinal
             self.gpu = str(cuda_index)
         self.proc = None

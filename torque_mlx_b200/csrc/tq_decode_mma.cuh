@@ -305,14 +305,23 @@ struct MmaCfg {
 // query rows; the barriers follow the ring.  STAGES is the largest count
 // (at most 4) that fits the CTA's share of the SM's shared memory: all of it
 // for one CTA per SM, half for two.
+#ifndef TQ_RING_TILES
+#define TQ_RING_TILES 2
+#endif
 template <int D, int BITS, int NT, int NW>
 struct RingCfg {
   using C = MmaCfg<D, BITS, NT, NW>;
-  static constexpr int TILE_WORDS = 16 * C::W;                    // one 16-token tile of one of K / V
-  static constexpr size_t STAGE_BYTES = 2 * (size_t)TILE_WORDS * 4;
   static constexpr size_t BUDGET = (NW == 16 || D == 256) ? 225 * 1024 : 112 * 1024;
   static constexpr size_t RING_OFF = (C::MAIN_BYTES + 127) / 128 * 128;
-  static constexpr size_t FIT = (BUDGET - RING_OFF - (size_t)NW * 4 * 8) / ((size_t)NW * STAGE_BYTES);
+  static constexpr size_t fit(int tiles) {
+    return (BUDGET - RING_OFF - (size_t)NW * 4 * 8) / ((size_t)NW * 2 * tiles * 16 * C::W * 4);
+  }
+  // tiles per stage: two (one wait, one refill and one pair of copies per 32
+  // tokens) when two such stages fit, else one
+  static constexpr int TILES = (TQ_RING_TILES >= 2 && fit(2) >= 2) ? 2 : 1;
+  static constexpr int TILE_WORDS = TILES * 16 * C::W;            // one stage of one of K / V
+  static constexpr size_t STAGE_BYTES = 2 * (size_t)TILE_WORDS * 4;
+  static constexpr size_t FIT = fit(TILES);
   static constexpr int STAGES = FIT > 4 ? 4 : (int)FIT;
   static_assert(FIT >= 2, "staging ring needs two slots per warp");
   static constexpr size_t BAR_OFF = RING_OFF + (size_t)NW * STAGES * STAGE_BYTES;
@@ -332,18 +341,19 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// Wait until the barrier's phase with this parity has completed; gives up
-// (false) after about a second of polling instead of spinning forever.
+// Wait until the barrier's phase with this parity has completed.  Each
+// try_wait suspends the warp in hardware until the phase completes or the
+// 100 us hint runs out, so a waiting warp issues almost nothing; after about
+// a second of attempts it gives up (false) instead of spinning forever.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t it = 0; it < (1u << 24); ++it) {
+  for (uint32_t it = 0; it < 10000u; ++it) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(done)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(100000u)
         : "memory");
     if (done) return true;
-    if (it >= 64) __nanosleep(64);
   }
   return false;
 }
@@ -594,22 +604,25 @@ decode_mma_kernel(DecodeParams p) {
   __syncwarp();
   const int64_t cap_rows = p.unit_stride / C::W;  // rows of the unit that may be read
   const int ntiles = w1 > w0 ? (int)((w1 - w0 + 15) / 16) : 0;
+  constexpr int TPS = RC::TILES;
+  constexpr int ROWS = TPS * 16;                   // token rows per stage
+  const int nstages = (ntiles + TPS - 1) / TPS;
   // tile i of the warp's range -> slot i % S.  Tiles start at multiples of 16
   // tokens, so both copies start on 16-byte boundaries; a whole tile is
   // copied when the unit's storage holds its 16 rows (rows past the length
   // are masked by the softmax), else the lanes copy the rows that exist.
   auto issue = [&](int i) {
     const int slot = i % S;
-    const int64_t t0 = w0 + 16 * (int64_t)i;
+    const int64_t t0 = w0 + ROWS * (int64_t)i;
     const uint32_t bar = bar0 + 8 * slot;
-    if (t0 + 16 <= cap_rows) {
+    if (t0 + ROWS <= cap_rows) {
       if (lane == 0) {
         mbar_expect_tx(bar, 2 * TW * 4);
         bulk_g2s(ring_s + slot * 2 * TW * 4, kbase + t0 * C::W, TW * 4, bar);
         bulk_g2s(ring_s + (slot * 2 + 1) * TW * 4, vbase + t0 * C::W, TW * 4, bar);
       }
     } else {
-      const int words = (int)min((int64_t)16, cap_rows - t0) * C::W;
+      const int words = (int)min((int64_t)ROWS, cap_rows - t0) * C::W;
       uint32_t* kd = ring + slot * 2 * TW;
       for (int w = lane; w < TW; w += 32) {
         kd[w] = w < words ? __ldcg(kbase + t0 * C::W + w) : 0u;
@@ -631,7 +644,7 @@ decode_mma_kernel(DecodeParams p) {
       __syncthreads();
     }
   }
-  for (int i = 0; i < S && i < ntiles; ++i) issue(i);  // in flight while the tables are built
+  for (int i = 0; i < S && i < nstages; ++i) issue(i);  // in flight while the tables are built
 
   // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
   {
@@ -696,23 +709,34 @@ decode_mma_kernel(DecodeParams p) {
   // token loop: wait for slot i % S, compute, refill the slot with tile i + S
   bool stalled = false;
   int i = 0;
-  for (; i < ntiles; ++i) {
-    const int slot = i % S;
-    if (!mbar_wait(bar0 + 8 * slot, (uint32_t)(i / S) & 1u)) {
-      stalled = true;
-      break;
+  // rounds of S stages, unrolled so every slot address is a constant offset
+  for (; i < nstages; i += S) {
+#pragma unroll
+    for (int slot = 0; slot < S; ++slot) {
+      const int st = i + slot;
+      if (st >= nstages) break;
+      if (!mbar_wait(bar0 + 8 * slot, (uint32_t)(st / S) & 1u)) {
+        stalled = true;
+        break;
+      }
+#pragma unroll
+      for (int sub = 0; sub < TPS; ++sub) {
+        const int64_t t0 = w0 + ROWS * (int64_t)st + 16 * sub;
+        if (sub > 0 && t0 >= w1) break;
+        TileRegs<D, BITS> t;
+        load_tile_smem<D, BITS>(t, ring + slot * 2 * TW + sub * 16 * C::W,
+                                ring + slot * 2 * TW + TW + sub * 16 * C::W, lp);
+        tile_math<D, BITS, NT>(t, (int)min((int64_t)16, w1 - t0), lut, lp, lane4, gr, tq, qf, o, mref, mthr, lrow);
+      }
+      __syncwarp();  // every lane has read the slot before it is refilled
+      if (st + S < nstages) issue(st + S);
     }
-    TileRegs<D, BITS> t;
-    load_tile_smem<D, BITS>(t, ring + slot * 2 * TW, ring + slot * 2 * TW + TW, lp);
-    tile_math<D, BITS, NT>(t, (int)min((int64_t)16, w1 - (w0 + 16 * (int64_t)i)), lut, lp, lane4, gr, tq, qf, o,
-                           mref, mthr, lrow);
-    __syncwarp();  // every lane has read the slot before it is refilled
-    if (i + S < ntiles) issue(i + S);
+    if (stalled) break;
   }
   if (stalled) {
     // a copy never completed: wait (bounded) for the ones still in flight so
     // none lands after the CTA's shared memory is reused, and poison the rows
-    for (int j = i; j < ntiles && j < i + S; ++j) mbar_wait(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
+    for (int j = i; j < nstages && j < i + 2 * S; ++j) mbar_wait(bar0 + 8 * (j % S), (uint32_t)(j / S) & 1u);
     s_fail = 1;
   }
 
