@@ -178,6 +178,9 @@ merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
                       const float* __restrict__ signs_left, const float* __restrict__ signs_right,
                       int32_t* __restrict__ advance, int64_t advance_n) {
   __shared__ float sm[MergeSmem<D, T>::FLOATS];
+  // launched as a programmatic dependent of the decode kernel: wait for its
+  // whole grid (and its memory) before reading a partial
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t row = blockIdx.x;
   merge_row<D, T>(part + row * nparts * (int64_t)(D + 2), nparts, out + row * D, lse ? lse + row : nullptr,
                   inverse_rotate, signs_left, signs_right, sm);
@@ -323,16 +326,36 @@ static void launch_decode_d(int bits, int mode, const DecodeParams& p, cudaStrea
   }
 }
 
+// The merge launches as a programmatic dependent of the decode kernel
+// (griddepcontrol): its CTAs are scheduled as the decode CTAs retire instead
+// of after the whole grid has drained, and each waits for the decode grid's
+// completion before reading a partial.
+template <typename... KArgs, typename... Args>
+static void launch_dependent(void (*kernel)(KArgs...), unsigned grid, unsigned block, cudaStream_t st,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <int D>
 static void launch_merge(const float* part, int nparts, int64_t rows, float* out, float* lse,
                          int inv, const float* sl, const float* sr, int32_t* adv, int64_t adv_n,
                          cudaStream_t st) {
   if (nparts >= kMergeWideParts)
-    merge_partials_kernel<D, kMergeWarpsWide * 32><<<(unsigned)rows, kMergeWarpsWide * 32, 0, st>>>(
-        part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
+    launch_dependent(merge_partials_kernel<D, kMergeWarpsWide * 32>, (unsigned)rows, kMergeWarpsWide * 32, st,
+                     part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
   else
-    merge_partials_kernel<D, kMergeWarps * 32><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(
-        part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
+    launch_dependent(merge_partials_kernel<D, kMergeWarps * 32>, (unsigned)rows, kMergeWarps * 32, st,
+                     part, nparts, rows, out, lse, inv, sl, sr, adv, adv_n);
 }
 
 template <int D>
@@ -340,11 +363,11 @@ static void launch_exchange(const float* part, int nparts, int64_t rows, const E
                             float* lse, int inv, const float* sl, const float* sr, int32_t* adv, int64_t adv_n,
                             cudaStream_t st) {
   if (nparts >= kMergeWideParts)
-    exchange_merge_kernel<D, kMergeWarpsWide * 32><<<(unsigned)rows, kMergeWarpsWide * 32, 0, st>>>(
-        part, nparts, rows, x, out, lse, inv, sl, sr, adv, adv_n);
+    launch_dependent(exchange_merge_kernel<D, kMergeWarpsWide * 32>, (unsigned)rows, kMergeWarpsWide * 32, st,
+                     part, nparts, rows, x, out, lse, inv, sl, sr, adv, adv_n);
   else
-    exchange_merge_kernel<D, kMergeWarps * 32><<<(unsigned)rows, kMergeWarps * 32, 0, st>>>(
-        part, nparts, rows, x, out, lse, inv, sl, sr, adv, adv_n);
+    launch_dependent(exchange_merge_kernel<D, kMergeWarps * 32>, (unsigned)rows, kMergeWarps * 32, st,
+                     part, nparts, rows, x, out, lse, inv, sl, sr, adv, adv_n);
 }
 
 // The new token of a fused append-and-decode step (tq_decode_append).

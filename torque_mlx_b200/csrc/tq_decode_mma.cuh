@@ -740,6 +740,8 @@ decode_mma_kernel(DecodeParams p) {
     s_fail = 1;
   }
 
+  // the split-merge grid may be scheduled as CTAs reach this point
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // ---- merge the warps of this CTA through shared memory (reusing the tables) ----
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)

@@ -71,6 +71,7 @@ exchange_merge_kernel(const float* __restrict__ part, int nparts, int64_t rows, 
   constexpr int64_t RF = exchange_row_floats(D);
   __shared__ float sm[MergeSmem<D, T>::FLOATS];
   __shared__ int s_ok;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the decode grid's partials are complete
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
   const uint32_t e = (uint32_t)x.epoch[row] + 1u;

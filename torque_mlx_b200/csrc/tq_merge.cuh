@@ -22,11 +22,17 @@ constexpr float kLn2 = 0.6931471805599453f;
 template <int D, int T>
 struct MergeSmem {
   static constexpr int SLICES = T / D;  // threads per output dim (parts split between them)
-  static constexpr int FLOATS = kMergeMaxParts + T + T / 32 + 2;
+  static constexpr int FLOATS = 2 * kMergeMaxParts + T + T / 32 + 2;
 };
 
 // part row layout: [nparts][D + 2] = (o[0..D), m, l), read through L2
-// (ld.global.cg: every partial is read once).
+// (ld.global.cg: every partial is read once).  One global round trip: each
+// thread issues the loads of its parts' (m, l) and, at the same time, of the
+// first kPrefetch o values it will weigh; the weights are formed in shared
+// memory once the row max is known, and only rows with more parts than the
+// prefetch covers go back to global memory for the rest.
+constexpr int kMergePrefetch = 16;
+
 template <int D, int T>
 __device__ __forceinline__ void merge_row(const float* __restrict__ base, int nparts, float* __restrict__ out_row,
                                           float* lse_row, int inverse_rotate, const float* signs_left,
@@ -36,19 +42,32 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
   constexpr int E = D / 32;
   constexpr int NWARP = T / 32;
   constexpr int SLICES = MergeSmem<D, T>::SLICES;
-  float* w_s = smem;                         // [kMergeMaxParts]
+  float* w_s = smem;                         // [kMergeMaxParts] m_i, then the weights
   float* acc_s = w_s + kMergeMaxParts;       // [SLICES][D]
   float* red = acc_s + T;                    // [NWARP]
   float* row_s = red + NWARP;                // M, L
+  float* l_s = row_s + 2;                    // [kMergeMaxParts] l_i
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int np = nparts < kMergeMaxParts ? nparts : kMergeMaxParts;
+  const int dim = tid % D, slice = tid / D;
   __syncthreads();  // smem may still be in use by the caller
 
-  // 1) max over parts that saw tokens
+  // 1) loads in flight together: (m, l) of parts tid, tid + T, ... and the o
+  //    values of parts slice, slice + SLICES, ... (the first kPrefetch)
+  float ov[kMergePrefetch];
+#pragma unroll
+  for (int k = 0; k < kMergePrefetch; ++k) {
+    const int i = slice + k * SLICES;
+    ov[k] = i < np ? __ldcg(base + (int64_t)i * (D + 2) + dim) : 0.f;
+  }
   float M = -INFINITY;
   for (int i = tid; i < np; i += T) {
     const float* pp = base + i * (int64_t)(D + 2);
-    if (__ldcg(pp + D + 1) > 0.f) M = fmaxf(M, __ldcg(pp + D));
+    const float mi = __ldcg(pp + D), li = __ldcg(pp + D + 1);
+    const bool seen = li > 0.f;
+    w_s[i] = seen ? mi : -INFINITY;
+    l_s[i] = li;
+    if (seen) M = fmaxf(M, mi);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
@@ -61,43 +80,42 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
   }
   __syncthreads();
   M = row_s[0];
-  // 2) per-part weights (0 for empty parts) and the denominator
+  // 2) weights from shared memory, and the denominator
   float L = 0.f;
   for (int i = tid; i < np; i += T) {
-    const float* pp = base + i * (int64_t)(D + 2);
-    const float li = __ldcg(pp + D + 1);
-    const float w = (li > 0.f && M != -INFINITY) ? exp2f(__ldcg(pp + D) - M) : 0.f;
+    const float mi = w_s[i];
+    const float w = (mi == -INFINITY || M == -INFINITY) ? 0.f : exp2f(mi - M);
     w_s[i] = w;
-    L += li * w;
+    L += l_s[i] * w;
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
-  __syncthreads();  // every warp has read red[] (step 1) before it is reused
+  __syncthreads();  // every warp has read red[] and w_s is complete
   if (lane == 0) red[warp] = L;
-  __syncthreads();
-  if (tid == 0) {
-    float l = 0.f;
-    for (int w = 0; w < NWARP; ++w) l += red[w];
-    row_s[1] = l;
+  // 3) weighted sum over the prefetched values, then any remaining parts
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMergePrefetch; k += 2) {
+    const int i = slice + k * SLICES;
+    if (i < np) a0 = fmaf(ov[k], w_s[i], a0);
+    if (i + SLICES < np) a1 = fmaf(ov[k + 1], w_s[i + SLICES], a1);
   }
-  // 3) weighted sum: thread (slice, dim) sums parts slice, slice + SLICES, ...
-  //    with four independent loads in flight
   {
-    const int dim = tid % D, slice = tid / D;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    int i = slice;
-    for (; i + 3 * SLICES < np; i += 4 * SLICES) {
-      a0 = fmaf(__ldcg(base + (int64_t)i * (D + 2) + dim), w_s[i], a0);
-      a1 = fmaf(__ldcg(base + (int64_t)(i + SLICES) * (D + 2) + dim), w_s[i + SLICES], a1);
-      a2 = fmaf(__ldcg(base + (int64_t)(i + 2 * SLICES) * (D + 2) + dim), w_s[i + 2 * SLICES], a2);
-      a3 = fmaf(__ldcg(base + (int64_t)(i + 3 * SLICES) * (D + 2) + dim), w_s[i + 3 * SLICES], a3);
+    int i = slice + kMergePrefetch * SLICES;
+    float a2 = 0.f, a3 = 0.f;
+    for (; i + SLICES < np; i += 2 * SLICES) {
+      a2 = fmaf(__ldcg(base + (int64_t)i * (D + 2) + dim), w_s[i], a2);
+      a3 = fmaf(__ldcg(base + (int64_t)(i + SLICES) * (D + 2) + dim), w_s[i + SLICES], a3);
     }
-    for (; i < np; i += SLICES) a0 = fmaf(__ldcg(base + (int64_t)i * (D + 2) + dim), w_s[i], a0);
-    acc_s[slice * D + dim] = (a0 + a1) + (a2 + a3);
+    if (i < np) a2 = fmaf(__ldcg(base + (int64_t)i * (D + 2) + dim), w_s[i], a2);
+    a0 += a2;
+    a1 += a3;
   }
+  acc_s[slice * D + dim] = a0 + a1;
   __syncthreads();
   if (warp == 0) {
-    const float Lsum = row_s[1];
+    float Lsum = 0.f;
+    for (int w = 0; w < NWARP; ++w) Lsum += red[w];
     float v[E];
 #pragma unroll
     for (int j = 0; j < E; ++j) {
