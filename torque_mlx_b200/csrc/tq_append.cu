@@ -20,6 +20,10 @@ constexpr int kAppendWarps = 8;  // rows per CTA
 // ---------------------------------------------------------------------------
 // rotate + quantize + pack one row per warp into the slab.
 // ---------------------------------------------------------------------------
+// Each warp takes kAppendRows consecutive rows and issues all their loads
+// before any math, so several rows' reads are in flight per warp.
+constexpr int kAppendRows = 4;
+
 template <int D, int BITS, typename T>
 __global__ void __launch_bounds__(kAppendWarps * 32)
 append_pack_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t groups, int tokens,
@@ -32,31 +36,38 @@ append_pack_kernel(const T* __restrict__ k, const T* __restrict__ v, int64_t gro
   constexpr int W = D * BITS / 32;
   constexpr int L = 1 << BITS;
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kAppendWarps + (threadIdx.x >> 5);
+  const int64_t row0 = ((int64_t)blockIdx.x * kAppendWarps + (threadIdx.x >> 5)) * kAppendRows;
   const int64_t rows = groups * (int64_t)tokens;
-  if (row >= rows) return;
+  if (row0 >= rows) return;
   const int which = blockIdx.y;  // 0 = K, 1 = V
   const T* x = which ? v : k;
   const float* cent = which ? cent_v : cent_k;
   uint32_t* slab = which ? v_slab : k_slab;
 
-  const int64_t g = row / tokens;
-  const int t = (int)(row - g * tokens);
-  int64_t pos = pos_offset + t;
-  if (start_pos) pos += start_pos[g / groups_per_seq];
-  if (pos < 0 || pos >= capacity) return;
-
+  float val[kAppendRows][E];
+#pragma unroll
+  for (int r = 0; r < kAppendRows; ++r) {
+    const int64_t row = row0 + r;
+    const T* src = x + (row < rows ? row : row0) * D;
+#pragma unroll
+    for (int j = 0; j < E; ++j) val[r][j] = to_f32(src[j * 32 + lane]);
+  }
   float c[L];
 #pragma unroll
   for (int i = 0; i < L; ++i) c[i] = __ldg(cent + i);
 
-  float val[E];
-  const T* src = x + row * D;
 #pragma unroll
-  for (int j = 0; j < E; ++j) val[j] = to_f32(src[j * 32 + lane]);
-  if (rotate) warp_rotate<D>(val, lane, signs_right, signs_left);
-
-  warp_pack_row<D, BITS>(val, lane, c, slab + g * group_stride + pos * W);
+  for (int r = 0; r < kAppendRows; ++r) {
+    const int64_t row = row0 + r;
+    if (row >= rows) break;
+    const int64_t g = row / tokens;
+    const int t = (int)(row - g * tokens);
+    int64_t pos = pos_offset + t;
+    if (start_pos) pos += start_pos[g / groups_per_seq];
+    if (pos < 0 || pos >= capacity) continue;  // warp-uniform
+    if (rotate) warp_rotate<D>(val[r], lane, signs_right, signs_left);
+    warp_pack_row<D, BITS>(val[r], lane, c, slab + g * group_stride + pos * W);
+  }
 }
 
 // Boundary-count quantize + pack of already-rotated fp32 rows, one row per
@@ -193,7 +204,8 @@ static void launch_append(const void* k, const void* v, int64_t groups, int toke
                           int64_t capacity, const int32_t* start, int gps, int64_t off,
                           cudaStream_t st) {
   const int64_t rows = groups * (int64_t)tokens;
-  dim3 grid((unsigned)((rows + kAppendWarps - 1) / kAppendWarps), v ? 2 : 1);
+  const int64_t per_cta = (int64_t)kAppendWarps * kAppendRows;
+  dim3 grid((unsigned)((rows + per_cta - 1) / per_cta), v ? 2 : 1);
   append_pack_kernel<D, BITS, T><<<grid, kAppendWarps * 32, 0, st>>>(
       (const T*)k, (const T*)v, groups, tokens, sl, sr, rotate, ck, cv, ks, vs, gstride, capacity,
       start, gps, off);

@@ -84,17 +84,20 @@ exchange_merge_kernel(const float* __restrict__ part, int nparts, int64_t rows, 
   merge_row<D, T>(part + row * nparts * (int64_t)(D + 2), nparts, mine, mine + D, 0, nullptr, nullptr, sm);
   // (merge_row ends with a barrier: the slot is complete and visible in the CTA)
 
-  // 2. copy it to every peer, then publish
-  for (int p = 0; p < x.world; ++p) {
-    if (p == x.rank) continue;
-    float* dst = x.bufs[p] + ((par * (int64_t)x.world + x.rank) * rows + row) * RF;
-    for (int i = tid; i < D + 1; i += T) dst[i] = mine[i];
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (tid < x.world) {
-    uint32_t* flags = reinterpret_cast<uint32_t*>(x.bufs[tid] + data);
-    st_release_sys(flags + (int64_t)x.rank * rows + row, e);
+  // 2. warp 0 copies it to every peer, makes its stores visible system-wide
+  //    and publishes (the other warps go straight to the wait)
+  if (tid < 32) {
+    for (int p = 0; p < x.world; ++p) {
+      if (p == x.rank) continue;
+      float* dst = x.bufs[p] + ((par * (int64_t)x.world + x.rank) * rows + row) * RF;
+      for (int i = tid; i < D + 1; i += 32) dst[i] = mine[i];
+    }
+    if (x.world > 1) __threadfence_system();
+    __syncwarp();
+    if (tid < x.world) {
+      uint32_t* flags = reinterpret_cast<uint32_t*>(x.bufs[tid] + data);
+      st_release_sys(flags + (int64_t)x.rank * rows + row, e);
+    }
   }
 
   // 3. wait for every rank's slot in this buffer (bounded)
