@@ -647,18 +647,16 @@ decode_mma_kernel(DecodeParams p) {
   for (int i = 0; i < S && i < nstages; ++i) issue(i);  // in flight while the tables are built
 
   // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
+  // 16-byte store idx covers entry idx / 16: K copies in its first 8 stores,
+  // V copies in the last 8.  Consecutive threads write consecutive 16 bytes,
+  // so the stores are free of bank conflicts.
   {
     constexpr int MASK = (1 << BITS) - 1;
-    for (int e = tid; e < C::NP; e += NW * 32) {
-      const uint32_t hk = pack_half2(__ldg(p.cent_k + (e & MASK)), __ldg(p.cent_k + ((e >> BITS) & MASK)));
-      const uint32_t hv = pack_half2(__ldg(p.cent_v + (e & MASK)), __ldg(p.cent_v + ((e >> BITS) & MASK)));
-      uint4* dk = reinterpret_cast<uint4*>(lut + e * 64);
-      uint4* dv = reinterpret_cast<uint4*>(lut + e * 64 + 32);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        dk[i] = make_uint4(hk, hk, hk, hk);
-        dv[i] = make_uint4(hv, hv, hv, hv);
-      }
+    for (int idx = tid; idx < C::NP * 16; idx += NW * 32) {
+      const int e = idx >> 4;
+      const float* cent = (idx & 15) < 8 ? p.cent_k : p.cent_v;
+      const uint32_t h = pack_half2(__ldg(cent + (e & MASK)), __ldg(cent + ((e >> BITS) & MASK)));
+      reinterpret_cast<uint4*>(lut)[idx] = make_uint4(h, h, h, h);
     }
   }
   // ---- query rows: rotate (exact fp32), fold the scale in base 2 ----

@@ -73,13 +73,10 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
   for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
   if (lane == 0) red[warp] = M;
   __syncthreads();
-  if (tid == 0) {
-    float m = -INFINITY;
-    for (int w = 0; w < NWARP; ++w) m = fmaxf(m, red[w]);
-    row_s[0] = m;
-  }
-  __syncthreads();
-  M = row_s[0];
+  // every warp reduces the per-warp maxima itself (no serial pass, no extra barrier)
+  M = lane < NWARP ? red[lane] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
   // 2) weights from shared memory, and the denominator
   float L = 0.f;
   for (int i = tid; i < np; i += T) {
@@ -114,8 +111,9 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
   acc_s[slice * D + dim] = a0 + a1;
   __syncthreads();
   if (warp == 0) {
-    float Lsum = 0.f;
-    for (int w = 0; w < NWARP; ++w) Lsum += red[w];
+    float Lsum = lane < NWARP ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) Lsum += __shfl_xor_sync(FULL, Lsum, o);
     float v[E];
 #pragma unroll
     for (int j = 0; j < E; ++j) {
