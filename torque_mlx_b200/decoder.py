@@ -2,8 +2,10 @@
 (benchmark config 5: the model around the packed-KV path).
 
 A plain pre-norm decoder (RMSNorm, RoPE, SwiGLU MLP, bf16 weights drawn from
-N(0, 0.02)) with one ``TorqueKVCache`` per layer.  Projections, norms and the
-MLP are ordinary cuBLAS / torch ops; the KV path is this library: prompt
+N(0, 0.02)) with one ``TorqueKVCache`` per layer.  In the token step the
+projections run as this library's one-token GEMV (tq_gemv, with RMSNorm /
+SwiGLU / fp32-input prologues), RoPE as tq_rope_qk; the dense prefill uses
+torch ops.  The KV path is this library too: prompt
 tokens are packed in bulk after a dense causal prefill, each generated token
 is packed and attended straight on the packed codes in one fused call
 (tq_decode_append).  The whole per-token step can be captured in one CUDA graph.
