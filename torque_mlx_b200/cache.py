@@ -424,12 +424,14 @@ class TorqueKVCache:
     decode_mlx_with_current = decode_with_current
 
     # ------------------------------------------------------------ CUDA graph
-    def capture_step(self, *, key, value, query) -> "CapturedDecodeStep":
+    def capture_step(self, *, key, value, query, steps_per_replay: int = 1) -> "CapturedDecodeStep":
         """Capture one decode step (append one token to every sequence, then
         attend) into CUDA graphs for launch-free replay.  ``key``/``value``/
         ``query`` are example CUDA tensors in the shapes ``append``/``decode``
-        take; their contents are copied into static input buffers."""
-        return CapturedDecodeStep(self, key=key, value=value, query=query)
+        take; their contents are copied into static input buffers.
+        ``steps_per_replay`` > 1 puts that many consecutive fused steps in the
+        ``step`` graph, so short steps are not bound by the host's replay rate."""
+        return CapturedDecodeStep(self, key=key, value=value, query=query, steps_per_replay=steps_per_replay)
 
     # ------------------------------------------------------------------ misc
     def export_dequantized(self) -> tuple[np.ndarray, np.ndarray]:
@@ -570,7 +572,10 @@ class CapturedDecodeStep:
     the two replays) until ``remaining`` reaches zero, then capture again.
     """
 
-    def __init__(self, cache: TorqueKVCache, *, key, value, query):
+    def __init__(self, cache: TorqueKVCache, *, key, value, query, steps_per_replay: int = 1):
+        if steps_per_replay < 1:
+            raise ValueError("steps_per_replay must be positive")
+        self.steps_per_replay = int(steps_per_replay)
         if not (isinstance(key, torch.Tensor) and key.is_cuda and isinstance(query, torch.Tensor) and query.is_cuda):
             raise ValueError("capture_step needs CUDA tensors")
         self.cache = cache
@@ -583,7 +588,7 @@ class CapturedDecodeStep:
         self.query = q.clone()
         self.out = torch.empty_like(self.query)
         self._hq = hq
-        cache._ensure_capacity(cache.sequence_length + 1)
+        cache._ensure_capacity(cache.sequence_length + self.steps_per_replay)
         stream = torch.cuda.Stream(device=cache._dev)
         stream.wait_stream(torch.cuda.current_stream(cache._dev))
         with torch.cuda.stream(stream):
@@ -599,8 +604,9 @@ class CapturedDecodeStep:
                 cache._decode(self.query, hq, extra=0, return_lse=False, full_capacity=True, out=self.out)
             self.g_step = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.g_step, stream=stream):
-                cache._step(self.key, self.value, self.query, hq, advance=True, return_lse=False,
-                            full_capacity=True, out=self.out)
+                for _ in range(self.steps_per_replay):  # lengths advance on the device between steps
+                    cache._step(self.key, self.value, self.query, hq, advance=True, return_lse=False,
+                                full_capacity=True, out=self.out)
         torch.cuda.current_stream(cache._dev).wait_stream(stream)
 
     @property
@@ -620,9 +626,10 @@ class CapturedDecodeStep:
 
     def step(self) -> torch.Tensor:
         """Append the static token and attend, as one fused replay
-        (tq_decode_append: the decode kernel packs the token)."""
-        if self.remaining < 1:
+        (tq_decode_append: the decode kernel packs the token); with
+        ``steps_per_replay`` = k, k such steps (the output is the last one's)."""
+        if self.remaining < self.steps_per_replay:
             raise RuntimeError("cache capacity reached: capture the step again")
         self.g_step.replay()
-        self.cache._len_host += 1
+        self.cache._len_host += self.steps_per_replay
         return self.out.reshape(self._out_shape)

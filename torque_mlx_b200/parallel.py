@@ -252,8 +252,10 @@ class SequenceShardedDecoder:
             self.cache.append(key=key, value=value)
         self.length += 1
 
-    def capture_step(self, key, value, query) -> None:
+    def capture_step(self, key, value, query, steps_per_replay: int = 1) -> None:
         """Capture one decode step for replay; needs ``plan.append_to_last``.
+        With the peer exchange, ``steps_per_replay`` > 1 captures that many
+        consecutive steps in one graph (every rank must use the same count).
 
         Two CUDA graphs around one eager collective: ``local`` (append on the
         owning rank, local decode, partials staged into the static
@@ -263,8 +265,9 @@ class SequenceShardedDecoder:
         resources.  Inputs are copied from the example tensors."""
         if not self.plan.append_to_last:
             raise ValueError("graph capture needs SequencePlan(append_to_last=True)")
+        self.steps_per_replay = 1
         if self.exchange == "peer":
-            return self._capture_peer(key, value, query)
+            return self._capture_peer(key, value, query, steps_per_replay)
         from . import ops
         c = self.cache
         self.owner = self.rank == self.world - 1
@@ -306,7 +309,7 @@ class SequenceShardedDecoder:
         torch.cuda.current_stream().wait_stream(side)
         assert self._out.shape == (rows, d)
 
-    def _capture_peer(self, key, value, query) -> None:
+    def _capture_peer(self, key, value, query, steps_per_replay: int) -> None:
         """One CUDA graph per rank holds the whole step: tq_decode_exchange
         (the last rank also packs the new token) — two kernel launches, with
         the exchange and the cross-rank merge on the device."""
@@ -317,7 +320,7 @@ class SequenceShardedDecoder:
         q, hq, self._qshape = c._norm_query(query)
         self._q = q.clone()
         self._out = torch.empty_like(self._q)
-        c._ensure_capacity(c.sequence_length + 1)
+        c._ensure_capacity(c.sequence_length + steps_per_replay)
         k = self._k if self.owner else None
         v = self._v if self.owner else None
         self._peer(self._q.shape[0])
@@ -333,9 +336,11 @@ class SequenceShardedDecoder:
         with torch.cuda.stream(side):
             self.g_step = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.g_step, stream=side, capture_error_mode="thread_local"):
-                self._peer_step(self._q, hq, k, v, full_capacity=True, out=self._out)
+                for _ in range(steps_per_replay):
+                    self._peer_step(self._q, hq, k, v, full_capacity=True, out=self._out)
         torch.cuda.current_stream().wait_stream(side)
         self.g_local = self.g_merge = None
+        self.steps_per_replay = steps_per_replay
 
     def _gather(self) -> None:
         if dist.get_backend(self.group) == "nccl":
@@ -346,13 +351,14 @@ class SequenceShardedDecoder:
     def step_graph(self):
         """One captured step: local graph, all-gather, merge graph.  Returns
         the merged output (a static buffer, overwritten by the next step)."""
-        if self.owner and self.cache.capacity - self.cache.sequence_length < 1:
+        n = self.steps_per_replay
+        if self.owner and self.cache.capacity - self.cache.sequence_length < n:
             raise RuntimeError("cache capacity reached: capture again")
         if self.exchange == "peer":
             self.g_step.replay()
             if self.owner:
-                self.cache._len_host += 1
-            self.length += 1
+                self.cache._len_host += n
+            self.length += n
             return self._out.reshape(self._qshape)
         self.g_local.replay()
         self._gather()
