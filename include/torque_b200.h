@@ -164,6 +164,25 @@ int tq_decode(const float* query, int rotate_query, const float* signs_left,
               float* lse, int inverse_rotate_output, int mode, void* workspace,
               size_t workspace_bytes, tq_stream_t stream);
 
+/* Chunked-prefill attention over packed codes: the last q_tokens tokens of
+ * each unit (already appended) are also queries, causally.  query is
+ * [units, q_tokens, group_size, head_dim] fp32 (token-major); row (t, g) of
+ * unit u attends positions [0, n_u - q_tokens + t + 1), with n_u as in
+ * tq_decode (lengths + len_offset, clamped to max_len).  out / lse have the
+ * query's row layout.  q_tokens * group_size <= 16 per call (a longer chunk is
+ * attended by successive calls, with len_offset moving the chunk's end).
+ * Runs on the tensor-core kernel; workspace as tq_decode_workspace_size with
+ * group_size = q_tokens * group_size and TQ_DECODE_TENSOR.
+ * Replaces the prefill attention of the reference's chunked-prefill loop
+ * (qwen_mlx.py:829-845, where it is dense attention over fresh K/V): here the
+ * chunk attends the packed cache, prefix and chunk alike. */
+int tq_decode_causal(const float* query, int rotate_query, const float* signs_left, const float* signs_right,
+                     const uint32_t* k_slab, const uint32_t* v_slab, int64_t unit_stride_words,
+                     const int32_t* lengths, int units_per_seq, int64_t len_offset, int64_t max_len, int64_t units,
+                     int q_tokens, int group_size, int head_dim, int bits, const float* cent_k,
+                     const float* cent_v, float scale, float* out, float* lse, int inverse_rotate_output,
+                     void* workspace, size_t workspace_bytes, tq_stream_t stream);
+
 /* One decode step with its append fused in: for every unit u of sequence
  * s = u / units_per_seq, row u of new_k / new_v ([units, head_dim] in kv_dtype)
  * is rotated (rotate_k / rotate_v), quantized with cent_k / cent_v and packed

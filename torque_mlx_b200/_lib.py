@@ -52,6 +52,9 @@ SIGNATURES: dict[str, tuple] = {
     "tq_decode": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
                           c_int64, c_int64, c_int64, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
                           c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "tq_decode_causal": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int,
+                                 c_int64, c_int64, c_int64, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_float,
+                                 c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "tq_decode_append": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int64, c_int64, c_int, c_int,
                                  c_int, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int, c_int, c_void_p,

@@ -423,6 +423,51 @@ class TorqueKVCache:
 
     decode_mlx_with_current = decode_with_current
 
+    def attend_chunk(self, *, query):
+        """Chunked-prefill attention on the packed cache: the last T tokens of
+        every sequence (appended already, e.g. by ``append``) attend causally,
+        each over the packed prefix and the chunk up to itself — the prefill
+        step of the reference's chunked loop (qwen_mlx.py:829-845), here over
+        packed codes.  ``query`` is ``[layers, T, Hq, d]`` (batch 1) or
+        ``[batch, layers, T, Hq, d]``; the result has its shape.  Runs as
+        ``tq_decode_causal`` launches of up to 16 query rows per kv head."""
+        cfg = self.config
+        np_out = _tensors.is_numpy(query)
+        t = _tensors.to_cuda(query, torch.float32)
+        shape = tuple(t.shape)
+        B, L, H, d = self.batch_size, cfg.num_layers, cfg.kv_heads, cfg.head_dim
+        if t.dim() == 4 and B == 1:
+            t = t.unsqueeze(0)
+        if t.dim() != 5 or t.shape[0] != B or t.shape[1] != L or t.shape[4] != d:
+            raise ValueError(f"query must have shape ({L}, T, query_heads, {d}) or ({B}, {L}, T, query_heads, {d}), "
+                             f"got {shape}")
+        T, hq = int(t.shape[2]), int(t.shape[3])
+        if hq % H != 0:
+            raise ValueError(f"query head count {hq} must be divisible by kv_heads {H}")
+        G = hq // H
+        if G > 16:
+            raise ValueError(f"query group size {G} exceeds 16")
+        if T < 1 or T > int(self._len_host.min()):
+            raise ValueError("attend_chunk needs 1 <= T <= every sequence's length (append the chunk first)")
+        q = t.reshape(B, L, T, H, G, d).permute(0, 1, 3, 2, 4, 5)  # [B, L, H, T, G, d]: unit-major rows
+        out = torch.empty_like(q)
+        units = B * L * H
+        step = max(1, 16 // G)
+        max_len = min(self._cap, self.sequence_length)
+        for j0 in range(0, T, step):
+            j1 = min(T, j0 + step)
+            qs = q[:, :, :, j0:j1].contiguous()
+            os_ = torch.empty_like(qs)
+            ops.decode_causal_raw(query=qs, k_slab=self._k, v_slab=self._v, unit_stride=self._cap * self._W,
+                                  lengths=self._len_dev, units_per_seq=L * H, len_offset=-(T - j1), max_len=max_len,
+                                  units=units, q_tokens=j1 - j0, group_size=G, head_dim=d, bits=cfg.bit_width,
+                                  cent_k=self._ck, cent_v=self._cv, out=os_, rotate_query=self.rotate_queries_on_decode,
+                                  inverse_rotate=not cfg.fused_weights, signs=self._signs,
+                                  scale=1.0 / sqrt(d), workspace=self._ws)
+            out[:, :, :, j0:j1] = os_
+        res = out.permute(0, 1, 3, 2, 4, 5).reshape(B, L, T, hq, d).reshape(shape)
+        return _tensors.out(res, np_out)
+
     # ------------------------------------------------------------ CUDA graph
     def capture_step(self, *, key, value, query, steps_per_replay: int = 1) -> "CapturedDecodeStep":
         """Capture one decode step (append one token to every sequence, then

@@ -415,7 +415,7 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
                        int bits, const float* cent_k, const float* cent_v, float scale, float* out,
                        float* lse, int inverse_rotate_output, int mode, void* workspace,
                        size_t workspace_bytes, tq_stream_t stream, const StepAppend* app,
-                       const ExchangeParams* xch = nullptr) {
+                       const ExchangeParams* xch = nullptr, int q_tokens = 1) {
   if (!valid_bits(bits)) return TQ_E_BITS;
   if (!valid_head_dim(head_dim)) return TQ_E_HEAD_DIM;
   if (units < 0 || group_size < 1 || group_size > 16 || max_len < 0) return TQ_E_SHAPE;
@@ -430,6 +430,10 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   if (!slabs_aligned(k_slab, v_slab, unit_stride_words)) {
     if (mode == TQ_DECODE_TENSOR) return TQ_E_SHAPE;
     mode = TQ_DECODE_EXACT;
+  }
+  if (q_tokens > 1) {
+    if (mode == TQ_DECODE_EXACT) return TQ_E_ARG;  // the causal chunk runs on the tensor-core kernel
+    mode = TQ_DECODE_TENSOR;
   }
   const Plan pl = make_plan(units, group_size, head_dim, bits, max_len, mode);
   if (!workspace || workspace_bytes < pl.bytes) return TQ_E_WORKSPACE;
@@ -465,6 +469,8 @@ static int decode_core(const float* query, int rotate_query, const float* signs_
   p.out = direct ? out : nullptr;
   p.lse = direct ? lse : nullptr;
   p.inverse_rotate = inverse_rotate_output;
+  p.q_tokens = q_tokens;
+  p.heads = group_size / (q_tokens > 0 ? q_tokens : 1);
 
   cudaStream_t st = (cudaStream_t)stream;
   if (app) {
@@ -587,6 +593,19 @@ int tq_decode_exchange(const void* new_k, const void* new_v, int kv_dtype, int r
   return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
                      units_per_seq, 1, max_len, units, group_size, head_dim, bits, cent_k, cent_v, scale, out, lse,
                      inverse_rotate_output, mode, workspace, workspace_bytes, stream, &app, &x);
+}
+
+int tq_decode_causal(const float* query, int rotate_query, const float* signs_left, const float* signs_right,
+                     const uint32_t* k_slab, const uint32_t* v_slab, int64_t unit_stride_words,
+                     const int32_t* lengths, int units_per_seq, int64_t len_offset, int64_t max_len, int64_t units,
+                     int q_tokens, int group_size, int head_dim, int bits, const float* cent_k,
+                     const float* cent_v, float scale, float* out, float* lse, int inverse_rotate_output,
+                     void* workspace, size_t workspace_bytes, tq_stream_t stream) {
+  if (q_tokens < 1 || group_size < 1 || q_tokens * group_size > 16) return TQ_E_SHAPE;
+  return decode_core(query, rotate_query, signs_left, signs_right, k_slab, v_slab, unit_stride_words, lengths,
+                     units_per_seq, len_offset, max_len, units, q_tokens * group_size, head_dim, bits, cent_k, cent_v,
+                     scale, out, lse, inverse_rotate_output, TQ_DECODE_TENSOR, workspace, workspace_bytes, stream,
+                     nullptr, nullptr, q_tokens);
 }
 
 int tq_lse_merge(const float* outs, const float* lses, int parts, int64_t rows, int head_dim,

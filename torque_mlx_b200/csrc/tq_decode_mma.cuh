@@ -72,6 +72,11 @@ struct DecodeParams {
   float* out;            // [units*G, D], null: partials to `part`
   float* lse;            // [units*G] or null
   int inverse_rotate;
+  // causal chunk attention (tq_decode_causal): the unit's last q_tokens
+  // tokens are also queries; query row g is token g / heads of the chunk and
+  // attends positions < n - q_tokens + g / heads + 1.  q_tokens <= 1: decode.
+  int q_tokens;
+  int heads;
 };
 
 // Length of unit u before clamping to max_len.
@@ -435,7 +440,8 @@ template <int D, int BITS, int NT>
 __device__ __forceinline__ void tile_math(const TileRegs<D, BITS>& t, int valid, const uint32_t* lut,
                                           const LanePlan& lp, uint32_t lane4, int gr, int tq,
                                           const uint32_t (&qf)[NT][D / 16][2], float (&o)[NT][D / 16][4],
-                                          float (&mref)[NT][2], float (&mthr)[NT][2], float (&lrow)[NT][2]) {
+                                          float (&mref)[NT][2], float (&mthr)[NT][2], float (&lrow)[NT][2],
+                                          int64_t causal_lim0 = 0, int64_t tpos = -1, int heads = 1) {
   using C = MmaCfg<D, BITS, NT>;
   constexpr int KB = C::KB;
   constexpr int PB = 2 * BITS;
@@ -477,6 +483,16 @@ __device__ __forceinline__ void tile_math(const TileRegs<D, BITS>& t, int valid,
         for (int e = 0; e < 4; ++e)
           if (!((e < 2) ? v0 : v1)) sc[nt][e] = -INFINITY;
     }
+    if (tpos >= 0 && tpos + 16 > causal_lim0) {  // tile reaches the causal chunk
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int g = nt * 8 + 2 * tq + (e & 1);
+          const int64_t pos = tpos + gr + ((e < 2) ? 0 : 8);
+          if (pos >= causal_lim0 + g / heads) sc[nt][e] = -INFINITY;
+        }
+    }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -491,7 +507,7 @@ __device__ __forceinline__ void tile_math(const TileRegs<D, BITS>& t, int valid,
           tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 8));
           tm = fmaxf(tm, __shfl_xor_sync(FULL, tm, 16));
           const float mn = fmaxf(mref[nt][e], tm);
-          const float alpha = fast_exp2(mref[nt][e] - mn);  // -inf -> 0
+          const float alpha = mn == -INFINITY ? 0.f : fast_exp2(mref[nt][e] - mn);  // -inf -> 0
           mref[nt][e] = mn;
           mthr[nt][e] = mn + kLazyMaxSlack;
           lrow[nt][e] *= alpha;
@@ -505,8 +521,14 @@ __device__ __forceinline__ void tile_math(const TileRegs<D, BITS>& t, int valid,
     uint32_t pb[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const float p0 = fast_exp2(sc[nt][0] - mref[nt][0]), p1 = fast_exp2(sc[nt][1] - mref[nt][1]);
-      const float p2 = fast_exp2(sc[nt][2] - mref[nt][0]), p3 = fast_exp2(sc[nt][3] - mref[nt][1]);
+      float p0 = fast_exp2(sc[nt][0] - mref[nt][0]), p1 = fast_exp2(sc[nt][1] - mref[nt][1]);
+      float p2 = fast_exp2(sc[nt][2] - mref[nt][0]), p3 = fast_exp2(sc[nt][3] - mref[nt][1]);
+      if (tpos >= 0) {  // causal: a head may not have seen any position yet (max still -inf)
+        p0 = sc[nt][0] == -INFINITY ? 0.f : p0;
+        p1 = sc[nt][1] == -INFINITY ? 0.f : p1;
+        p2 = sc[nt][2] == -INFINITY ? 0.f : p2;
+        p3 = sc[nt][3] == -INFINITY ? 0.f : p3;
+      }
       const __half2 lo = __floats2half2_rn(p0, p1);
       const __half2 hi = __floats2half2_rn(p2, p3);
       lrow[nt][0] += p0 + p2;
@@ -724,7 +746,11 @@ decode_mma_kernel(DecodeParams p) {
         TileRegs<D, BITS> t;
         load_tile_smem<D, BITS>(t, ring + slot * 2 * TW + sub * 16 * C::W,
                                 ring + slot * 2 * TW + TW + sub * 16 * C::W, lp);
-        tile_math<D, BITS, NT>(t, (int)min((int64_t)16, w1 - t0), lut, lp, lane4, gr, tq, qf, o, mref, mthr, lrow);
+        if (p.q_tokens > 1)
+          tile_math<D, BITS, NT>(t, (int)min((int64_t)16, w1 - t0), lut, lp, lane4, gr, tq, qf, o, mref, mthr, lrow,
+                                 n - p.q_tokens + 1, t0, p.heads);
+        else
+          tile_math<D, BITS, NT>(t, (int)min((int64_t)16, w1 - t0), lut, lp, lane4, gr, tq, qf, o, mref, mthr, lrow);
       }
       __syncwarp();  // every lane has read the slot before it is refilled
       if (st + S < nstages) issue(st + S);

@@ -91,6 +91,27 @@ def decode_raw(*, query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tenso
     _lib.check(lib.tq_decode(*args), "decode")
 
 
+def decode_causal_raw(*, query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tensor, unit_stride: int,
+                      lengths: torch.Tensor, units_per_seq: int, len_offset: int, max_len: int, units: int,
+                      q_tokens: int, group_size: int, head_dim: int, bits: int, cent_k: torch.Tensor,
+                      cent_v: torch.Tensor, out: torch.Tensor, lse: torch.Tensor | None = None,
+                      rotate_query: bool = False, inverse_rotate: bool = False,
+                      signs: tuple[torch.Tensor, torch.Tensor] | None = None, scale: float | None = None,
+                      workspace: Workspace | None = None) -> None:
+    """One ``tq_decode_causal`` call: the last ``q_tokens`` tokens of every
+    unit attend causally (query ``[units, q_tokens, group_size, d]``)."""
+    lib = _lib.load()
+    wsp = workspace or _default_ws
+    sl, sr = signs if signs is not None else (None, None)
+    ws = wsp.get(workspace_bytes(units, q_tokens * group_size, head_dim, bits, max_len, "tensor"), out.device)
+    _lib.check(lib.tq_decode_causal(
+        query.data_ptr(), int(rotate_query), _lib.ptr(sl), _lib.ptr(sr), k_slab.data_ptr(), v_slab.data_ptr(),
+        unit_stride, lengths.data_ptr(), units_per_seq, len_offset, max_len, units, q_tokens, group_size, head_dim,
+        bits, cent_k.data_ptr(), cent_v.data_ptr(), float(1.0 / sqrt(head_dim) if scale is None else scale),
+        out.data_ptr(), _lib.ptr(lse), int(inverse_rotate), ws.data_ptr(), ws.numel(), _lib.stream_ptr()),
+        "decode_causal")
+
+
 def decode_append_raw(*, new_k: torch.Tensor, new_v: torch.Tensor, rotate_k: bool, rotate_v: bool, advance: bool,
                       query: torch.Tensor, k_slab: torch.Tensor, v_slab: torch.Tensor, unit_stride: int,
                       lengths: torch.Tensor, units_per_seq: int, max_len: int, units: int, group_size: int,
