@@ -115,3 +115,34 @@ def test_sequence_sharded_decode_matches_oracle(exchange):
     errs = dict(qu.get(timeout=5) for _ in range(world))
     # tensor-mode decode (fp16 operands) against the float64 oracle
     assert max(errs.values()) < 4e-3, errs
+
+
+def test_one_process_two_devices():
+    """One process decoding on two GPUs in turn: the kernels' shared-memory
+    opt-in and occupancy are per device, so the second device's launches are
+    as valid as the first's (needs two visible GPUs)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torque_mlx_b200 as T
+    from oracle import torque_oracle as O
+
+    rng = np.random.default_rng(2)
+    keys = rng.standard_normal((2, 3000, 128)).astype(np.float16)
+    vals = rng.standard_normal((2, 3000, 128)).astype(np.float16)
+    qry = rng.standard_normal((8, 128)).astype(np.float32)
+    outs = []
+    for dev in (0, 1, 0):
+        with torch.cuda.device(dev):
+            cache = T.TorqueKVCache(config=T.TorqueConfig(bit_width=4, head_dim=128, kv_heads=2),
+                                    decode_mode="tensor")
+            cache.append(key=keys, value=vals)
+            outs.append(cache.decode(query=qry))
+            if dev == 1:
+                kw, vw = cache.packed_words()
+                sl, sr = O.rotation_signs(128, 0)
+                o, _ = O.gqa_decode(O.rotate(qry, sl, sr)[None], kw[0][None], vw[0][None],
+                                    cache.key_codebook.centroids, cache.value_codebook.centroids, 4)
+                np.testing.assert_allclose(outs[-1], O.rotate_inverse(o[0].astype(np.float32), sl, sr),
+                                           atol=4e-3, rtol=2e-2)
+    np.testing.assert_array_equal(outs[0], outs[1])
+    np.testing.assert_array_equal(outs[0], outs[2])
