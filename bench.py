@@ -235,7 +235,8 @@ def build_cache(wl: dict, rank: int, torch, T, extra: int = 256, fused_weights: 
     B = wl["batch"]
     cfg = T.TorqueConfig(bit_width=wl["bits"], head_dim=wl["head_dim"], num_layers=1, kv_heads=wl["kv_heads"],
                          rotation_seed=0, fused_weights=fused_weights)
-    cache = T.TorqueKVCache(config=cfg, batch_size=B, initial_capacity=int(lens.max()) + extra)
+    cache = T.TorqueKVCache(config=cfg, batch_size=B, initial_capacity=int(lens.max()) + extra,
+                            decode_mode=wl.get("decode_mode", "auto"))
     gen = torch.Generator(device=dev)
     gen.manual_seed(wl["seed"] * 7919 + rank)
     H, d = wl["kv_heads"], wl["head_dim"]
@@ -686,11 +687,14 @@ def main() -> None:
     ap.add_argument("--no-extra", action="store_true", help="skip the extra N=1 workloads")
     ap.add_argument("--seq-steps", type=int, default=3000)
     ap.add_argument("--batch", type=int, default=None, help="override the per-GPU batch (small profiling cases)")
+    ap.add_argument("--decode-mode", default="auto", choices=["auto", "tensor", "exact"],
+                    help="decode kernel (exact: the fp32 CUDA-core kernel, for the tensor-core comparison)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = dict(WORKLOADS[args.workload])
     if args.batch:
         wl["batch"] = args.batch
+    wl["decode_mode"] = args.decode_mode
     if args.steps is None:
         args.steps = wl["steps"] if args.impl == "ours" else 5
     if args.impl == "reference":
