@@ -596,7 +596,11 @@ def run_ours(args, wl) -> None:
     e2e_value = B * world / (e2e_ms / 1e3)
     seq = None
     if not args.no_seq_split:
-        seq = measure_seq_split(torch, T, dist, args.seq_steps, args.warmup, rank, world)
+        try:
+            seq = measure_seq_split(torch, T, dist, args.seq_steps, args.warmup, rank, world)
+        except Exception as exc:  # noqa: BLE001 - the batch-shard line stands on its own
+            seq = {"workload": "config3", "n_gpus": world, "error": f"{type(exc).__name__}: {exc}"[:300]}
+            torch.cuda.synchronize()
     extra = {}
     if world == 1 and not args.no_extra:
         peak, _ = _peaks()
