@@ -409,3 +409,35 @@ def test_append_decode_many_units(b):
     np.testing.assert_allclose(got.cpu().numpy(), ref.decode(query=q).cpu().numpy(), atol=1e-6, rtol=1e-6)
     for a, c in zip(fused.packed_words(), ref.packed_words()):
         np.testing.assert_array_equal(a, c)
+
+
+def test_captured_step_run_from_host_buffers():
+    """CapturedDecodeStep.run copies each step's inputs (pinned host or device
+    tensors) into the static buffers and replays: same outputs and words as
+    eager append_decode on a twin cache."""
+    rng = np.random.default_rng(17)
+    B, L, H, G, d, b = 2, 1, 2, 4, 128, 3
+    cfg = T.TorqueConfig(bit_width=b, head_dim=d, num_layers=L, kv_heads=H)
+    cap = T.TorqueKVCache(config=cfg, batch_size=B, initial_capacity=1024)
+    ref = T.TorqueKVCache(config=cfg, batch_size=B, initial_capacity=1024)
+    for s, n in enumerate((300, 77)):
+        k = rng.standard_normal((L, H, n, d)).astype(np.float16)
+        v = rng.standard_normal((L, H, n, d)).astype(np.float16)
+        cap.append_sequence(s, key=k, value=v)
+        ref.append_sequence(s, key=k, value=v)
+    ex = torch.zeros((B, L, H, d), dtype=torch.float16, device="cuda")
+    step = cap.capture_step(key=ex, value=ex, query=torch.zeros((B, L, H * G, d), device="cuda"))
+    for i in range(4):
+        nk = torch.from_numpy(rng.standard_normal((B, L, H, d)).astype(np.float16))
+        nv = torch.from_numpy(rng.standard_normal((B, L, H, d)).astype(np.float16))
+        q = torch.from_numpy(rng.standard_normal((B, L, H * G, d)).astype(np.float32))
+        if i % 2 == 0:
+            nk, nv, q = nk.pin_memory(), nv.pin_memory(), q.pin_memory()
+        else:
+            nk, nv, q = nk.cuda(), nv.cuda(), q.cuda()
+        got = step.run(key=nk, value=nv, query=q).clone()
+        want = ref.append_decode(key=nk.cuda(), value=nv.cuda(), query=q.cuda())
+        np.testing.assert_allclose(got.reshape(want.shape).cpu().numpy(), want.cpu().numpy(), atol=1e-6, rtol=1e-6)
+    assert list(cap.lengths) == list(ref.lengths)
+    for a, c in zip(cap.packed_words(), ref.packed_words()):
+        np.testing.assert_array_equal(a, c)

@@ -669,6 +669,20 @@ class CapturedDecodeStep:
         self.g_decode.replay()
         return self.out.reshape(self._out_shape)
 
+    def run(self, *, key, value, query) -> torch.Tensor:
+        """Serving form of a captured step: copy this step's new key/value and
+        query (same shapes as at capture; host tensors - pinned for an
+        asynchronous copy - or device tensors) into the static input buffers on
+        the current stream, then replay one fused step.  Returns the static
+        output buffer (overwritten by the next step; copy it out before)."""
+        if self.steps_per_replay != 1:
+            raise ValueError("run() needs a step captured with steps_per_replay=1")
+        for dst, src, name in ((self.key, key, "key"), (self.value, value, "value"), (self.query, query, "query")):
+            if not isinstance(src, torch.Tensor) or src.numel() != dst.numel():
+                raise ValueError(f"{name} must be a tensor with {dst.numel()} elements, as at capture")
+            dst.view(-1).copy_(src.reshape(-1), non_blocking=True)
+        return self.step()
+
     def step(self) -> torch.Tensor:
         """Append the static token and attend, as one fused replay
         (tq_decode_append: the decode kernel packs the token); with
