@@ -437,7 +437,9 @@ def test_captured_step_run_from_host_buffers():
             nk, nv, q = nk.cuda(), nv.cuda(), q.cuda()
         got = step.run(key=nk, value=nv, query=q).clone()
         want = ref.append_decode(key=nk.cuda(), value=nv.cuda(), query=q.cuda())
-        np.testing.assert_allclose(got.reshape(want.shape).cpu().numpy(), want.cpu().numpy(), atol=1e-6, rtol=1e-6)
+        # the captured plan is sized for the capacity, the eager one for the
+        # length, so the split boundaries (and fp16 rounding points) differ
+        np.testing.assert_allclose(got.reshape(want.shape).cpu().numpy(), want.cpu().numpy(), **TOL["tensor"])
     assert list(cap.lengths) == list(ref.lengths)
     for a, c in zip(cap.packed_words(), ref.packed_words()):
         np.testing.assert_array_equal(a, c)
