@@ -213,7 +213,17 @@ __device__ __forceinline__ T ld_run(const T* p) {
   else return load_code(p);
 }
 
-template <int NB, int W, bool SMEM = false>
+// Whether any of the COUNT lane runs of NB bits (lane k starts at bit k*NB)
+// reaches one word past its first NW words; when none can, the tail load and
+// its branch are dropped at compile time (3-bit d128 V runs, for one).
+template <int NB, int COUNT>
+constexpr bool may_tail() {
+  for (int k = 0; k < COUNT; ++k)
+    if (((k * NB) & 31) + NB > 32 * Run<NB>::NW) return true;
+  return false;
+}
+
+template <int NB, int W, bool SMEM = false, bool TAIL = true>
 __device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const uint32_t* row, int start) {
   constexpr int NW = Run<NB>::NW;
   if constexpr (Run<NB>::ALIGNED) {
@@ -231,11 +241,12 @@ __device__ __forceinline__ void load_raw(uint32_t (&raw)[Run<NB>::RAW], const ui
       }
     }
   } else {
-    const bool tail = start + NB > 32 * NW;  // the run reaches one more word
 #pragma unroll
     for (int i = 0; i < NW; ++i) raw[i] = ld_run<SMEM>(row + i);
     raw[NW] = 0u;
-    if (tail) raw[NW] = ld_run<SMEM>(row + NW);
+    if constexpr (TAIL) {
+      if (start + NB > 32 * NW) raw[NW] = ld_run<SMEM>(row + NW);  // the run reaches one more word
+    }
   }
 }
 
@@ -410,12 +421,13 @@ __device__ __forceinline__ void load_tile_smem(TileRegs<D, BITS>& t, const uint3
                                                const LanePlan& lp) {
   using C = MmaCfg<D, BITS, 1>;
   constexpr int W = C::W;
-  load_raw<C::RUNK, W, true>(t.k0, kt + lp.k_row, lp.k_bit);
-  load_raw<C::RUNK, W, true>(t.k1, kt + lp.k_row + 8 * W, lp.k_bit);
-  load_raw<C::RUNV, W, true>(t.va, vt + lp.v_row, lp.v_bit);
-  load_raw<C::RUNV, W, true>(t.vb, vt + lp.v_row + W, lp.v_bit);
-  load_raw<C::RUNV, W, true>(t.vc, vt + lp.v_row + 8 * W, lp.v_bit);
-  load_raw<C::RUNV, W, true>(t.vd, vt + lp.v_row + 9 * W, lp.v_bit);
+  constexpr bool TK = may_tail<C::RUNK, 4>(), TV = may_tail<C::RUNV, 8>();
+  load_raw<C::RUNK, W, true, TK>(t.k0, kt + lp.k_row, lp.k_bit);
+  load_raw<C::RUNK, W, true, TK>(t.k1, kt + lp.k_row + 8 * W, lp.k_bit);
+  load_raw<C::RUNV, W, true, TV>(t.va, vt + lp.v_row, lp.v_bit);
+  load_raw<C::RUNV, W, true, TV>(t.vb, vt + lp.v_row + W, lp.v_bit);
+  load_raw<C::RUNV, W, true, TV>(t.vc, vt + lp.v_row + 8 * W, lp.v_bit);
+  load_raw<C::RUNV, W, true, TV>(t.vd, vt + lp.v_row + 9 * W, lp.v_bit);
 }
 
 // Tile that runs past the unit's last token: rows are clamped to `last`
