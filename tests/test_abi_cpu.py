@@ -75,3 +75,14 @@ def test_compute_path_fails_loudly_without_gpu(built_lib):
         quantize(np.zeros(4, np.float32), cb)
     with pytest.raises(RuntimeError, match="CUDA device"):
         TorqueKVCache(config=TorqueConfig(bit_width=4, head_dim=64))
+
+
+def test_bench_arms_print_the_same_config():
+    """bench.py's own arm and its --impl reference arm describe a workload with
+    the same config dict (the driver compares them)."""
+    import bench
+    for name in ("config4", "config4_4bit", "config3", "longctx128"):
+        wl = dict(bench.WORKLOADS[name])
+        for world in (1, 2, 8):
+            assert bench.config_dict(name, wl, world) == bench.config_dict(name, dict(wl), world)
+            assert bench.config_dict(name, wl, world)["global_batch"] == wl["batch"] * world

@@ -8,15 +8,20 @@ The reference runs on one device only; these partitions are new.
 
 * Sequence sharding (benchmark config 3, long batch-1 contexts): each rank
   owns a contiguous share of the prefill tokens plus the new tokens it is
-  assigned (round robin, or all on the last rank for graph-captured steps).  A decode step is
-      local tq_decode over the rank's tokens -> (o_r rotated, lse_r)
-      all-gather of [o_r | lse_r] over the process group (NCCL over NVLink)
-      tq_lse_merge:  o = sum_r exp(lse_r - LSE) o_r  (then Pi^T)
-  which equals attention over the union of the shards.
+  assigned (round robin, or all on the last rank for graph-captured steps).
+  With ``exchange="peer"`` (the default) a step is one ``tq_decode_exchange``
+  call per rank: the rank's shard decode, then a merge kernel that stores the
+  rank's normalised partial (o_r, lse_r) into every rank's exchange buffer
+  over NVLink (CUDA IPC mappings, ``PeerExchange``), publishes it with a
+  system-scope flag, waits (bounded) for the other ranks' flags and merges
+      o = sum_r exp(lse_r - LSE) o_r  (then Pi^T)
+  which equals attention over the union of the shards.  No host round trip
+  and no library collective in the step; one CUDA graph per step per rank.
+  ``exchange="nccl"`` keeps the all-gather variant: local decode, NCCL
+  all-gather of [o_r | lse_r], ``tq_lse_merge``.
 
-Everything here that is not a kernel launch (the token plan, packing the
-exchange buffer, the all-gather) is plain torch.distributed and is tested on
-CPU with gloo ranks; the merge itself is ``tq_lse_merge`` on the GPU.
+The token plan and the all-gather exchange are plain torch.distributed and are
+tested on CPU with gloo ranks; the peer exchange is tested on GPUs.
 """
 
 from __future__ import annotations
