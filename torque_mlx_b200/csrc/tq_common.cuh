@@ -10,6 +10,22 @@
 
 namespace tq {
 
+// Optional step timeline for development builds (-DTQ_TRACE): thread 0 of a
+// CTA records %globaltimer at fixed points into a per-file device array.
+#ifdef TQ_TRACE
+#define TQ_STAMP(arr, idx)                                                 \
+  do {                                                                     \
+    if (threadIdx.x == 0) {                                                \
+      unsigned long long t_;                                               \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));               \
+      arr[idx] = t_;                                                       \
+    }                                                                      \
+  } while (0)
+#else
+#define TQ_STAMP(arr, idx) do { } while (0)
+#endif
+
+
 constexpr unsigned FULL = 0xffffffffu;
 
 // ---------------------------------------------------------------------------
@@ -90,6 +106,25 @@ __device__ __forceinline__ void warp_rotate(float (&v)[D / 32], int lane, const 
 #pragma unroll
   for (int j = 0; j < E; ++j)
     v[j] = __fmul_rn(__fdiv_rn(v[j], SqrtD<D>::v), __ldg(second + j * 32 + lane));
+}
+
+// The same rotation with the sign vectors already in registers (loaded by
+// load_signs ahead of time, so their latency overlaps other work).
+template <int D>
+__device__ __forceinline__ void load_signs(float (&s)[D / 32], const float* p, int lane) {
+#pragma unroll
+  for (int j = 0; j < D / 32; ++j) s[j] = __ldg(p + j * 32 + lane);
+}
+
+template <int D>
+__device__ __forceinline__ void warp_rotate_regs(float (&v)[D / 32], int lane, const float (&first)[D / 32],
+                                                 const float (&second)[D / 32]) {
+  constexpr int E = D / 32;
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = __fmul_rn(v[j], first[j]);
+  warp_fwht<D>(v, lane);
+#pragma unroll
+  for (int j = 0; j < E; ++j) v[j] = __fmul_rn(__fdiv_rn(v[j], SqrtD<D>::v), second[j]);
 }
 
 // argmin_k |x - c[k]| over fp32 rounded distances, first index on ties.

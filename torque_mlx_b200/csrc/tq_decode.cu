@@ -180,12 +180,19 @@ merge_partials_kernel(const float* __restrict__ part, int nparts, int64_t rows,
   __shared__ float sm[MergeSmem<D, T>::FLOATS];
   // launched as a programmatic dependent of the decode kernel: wait for its
   // whole grid (and its memory) before reading a partial
+  TQ_MSTAMP(0);
+  // the next step's decode grid may be scheduled now; it waits for this grid
+  // to complete before it reads or writes global memory
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  TQ_MSTAMP(1);
   const int64_t row = blockIdx.x;
   merge_row<D, T>(part + row * nparts * (int64_t)(D + 2), nparts, out + row * D, lse ? lse + row : nullptr,
                   inverse_rotate, signs_left, signs_right, sm);
+  TQ_MSTAMP(2);
   if (advance && row == 0)
     for (int64_t i = threadIdx.x; i < advance_n; i += T) advance[i] += 1;
+  TQ_MSTAMP(3);
 }
 
 // ---------------------------------------------------------------------------
@@ -694,3 +701,11 @@ int tq_decode_static(const float* query, int rotate_query, const float* signs_le
 }
 
 }  // extern "C"
+
+#ifdef TQ_TRACE
+// Development builds only: copy the merge kernels' step timeline to the host.
+extern "C" int tq_trace_read_merge(void* host, size_t bytes) {
+  const size_t n = bytes < sizeof(tq::g_trace_mrg) ? bytes : sizeof(tq::g_trace_mrg);
+  return cudaMemcpyFromSymbol(host, tq::g_trace_mrg, n) == cudaSuccess ? 0 : -1;
+}
+#endif

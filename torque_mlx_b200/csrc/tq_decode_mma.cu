@@ -48,30 +48,47 @@ static int occupancy() {
   return blocks;
 }
 
+// The decode grid is a programmatic dependent of whatever kernel precedes it
+// on the stream: its CTAs may be scheduled while that kernel finishes (the
+// previous step's split merge calls griddepcontrol.launch_dependents on
+// entry), and the kernel waits (griddepcontrol.wait) before it reads any
+// global memory, so the launch latency between steps is hidden.
 template <int D, int BITS, int NT, int NW>
 static void launch_one(const DecodeParams& p, cudaStream_t st) {
-  dim3 grid(p.splits, (unsigned)p.units);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, (unsigned)p.units);
+  cfg.blockDim = dim3(NW * 32);
+  cfg.dynamicSmemBytes = RingCfg<D, BITS, NT, NW>::SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   prepare<D, BITS, NT, NW>();
-  decode_mma_kernel<D, BITS, NT, NW><<<grid, NW * 32, RingCfg<D, BITS, NT, NW>::SMEM_BYTES, st>>>(p);
+  cudaLaunchKernelEx(&cfg, decode_mma_kernel<D, BITS, NT, NW>, p);
 }
 
 template <int D, int BITS>
 static void launch_mma(const DecodeParams& p, cudaStream_t st) {
-  const bool wide = D <= 128 && p.nw == kMmaWarpsWide;
-  if (p.G <= 8) {
-    if (wide) launch_one<D, BITS, 1, kMmaWarpsWide>(p, st);
-    else launch_one<D, BITS, 1, kMmaWarps>(p, st);
-  } else {
-    if (wide) launch_one<D, BITS, 2, kMmaWarpsWide>(p, st);
-    else launch_one<D, BITS, 2, kMmaWarps>(p, st);
+  // wide CTAs exist for d <= 128 only (the planner never picks them for d = 256)
+  if constexpr (D <= 128) {
+    if (p.nw == kMmaWarpsWide) {
+      if (p.G <= 8) launch_one<D, BITS, 1, kMmaWarpsWide>(p, st);
+      else launch_one<D, BITS, 2, kMmaWarpsWide>(p, st);
+      return;
+    }
   }
+  if (p.G <= 8) launch_one<D, BITS, 1, kMmaWarps>(p, st);
+  else launch_one<D, BITS, 2, kMmaWarps>(p, st);
 }
 
 template <int D, int BITS>
 static int blocks_for(int G, int nw) {
-  const bool wide = D <= 128 && nw == kMmaWarpsWide;
-  if (G <= 8) return wide ? occupancy<D, BITS, 1, kMmaWarpsWide>() : occupancy<D, BITS, 1, kMmaWarps>();
-  return wide ? occupancy<D, BITS, 2, kMmaWarpsWide>() : occupancy<D, BITS, 2, kMmaWarps>();
+  if constexpr (D <= 128) {
+    if (nw == kMmaWarpsWide) return G <= 8 ? occupancy<D, BITS, 1, kMmaWarpsWide>() : occupancy<D, BITS, 2, kMmaWarpsWide>();
+  }
+  return G <= 8 ? occupancy<D, BITS, 1, kMmaWarps>() : occupancy<D, BITS, 2, kMmaWarps>();
 }
 
 #define TQ_DISPATCH(D_, bits_, CALL)                                   \
@@ -100,3 +117,16 @@ int mma_blocks_per_sm(int D, int bits, int G, int nw) {
 }
 
 }  // namespace tq
+
+#ifdef TQ_TRACE
+// Development builds only: copy the decode kernels' step timeline to the host.
+extern "C" int tq_trace_read_decode(void* host, size_t bytes) {
+  const size_t n = bytes < sizeof(tq::g_trace_dec) ? bytes : sizeof(tq::g_trace_dec);
+  return cudaMemcpyFromSymbol(host, tq::g_trace_dec, n) == cudaSuccess ? 0 : -1;
+}
+extern "C" int tq_trace_clear_decode() {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, tq::g_trace_dec) != cudaSuccess) return -1;
+  return cudaMemset(p, 0, sizeof(tq::g_trace_dec)) == cudaSuccess ? 0 : -1;
+}
+#endif

@@ -37,6 +37,14 @@
 
 namespace tq {
 
+#ifdef TQ_TRACE
+constexpr int kTraceCtas = 8192;
+static __device__ unsigned long long g_trace_dec[kTraceCtas * 8];
+#define TQ_DSTAMP(k) TQ_STAMP(g_trace_dec, ((blockIdx.y * gridDim.x + blockIdx.x) % kTraceCtas) * 8 + (k))
+#else
+#define TQ_DSTAMP(k) do { } while (0)
+#endif
+
 struct DecodeParams {
   const float* query;
   const float* signs_left;
@@ -599,6 +607,13 @@ decode_mma_kernel(DecodeParams p) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int gr = lane >> 2, tq = lane & 3;
   if (tid == 0) s_fail = 0;  // published by the table barrier below
+  TQ_DSTAMP(0);
+  // The grid is launched as a programmatic dependent of the previous kernel
+  // on the stream (the previous step's split merge): wait for that grid and
+  // its memory before reading the lengths, queries or slabs, or writing the
+  // partials it may still be reading.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  TQ_DSTAMP(1);
   const int64_t u = blockIdx.y;
   const int split = blockIdx.x;
   const int G = p.G;
@@ -676,9 +691,11 @@ decode_mma_kernel(DecodeParams p) {
       // that read them are async-proxy operations
       asm volatile("fence.proxy.async.global;" ::: "memory");
       __syncthreads();
+      TQ_DSTAMP(7);
     }
   }
   for (int i = 0; i < S && i < nstages; ++i) issue(i);  // in flight while the tables are built
+  TQ_DSTAMP(2);
 
   // ---- pair tables: entry e = half2(c[e & m], c[e >> b]), one copy per lane ----
   // 16-byte store idx covers entry idx / 16: K copies in its first 8 stores,
@@ -709,6 +726,7 @@ decode_mma_kernel(DecodeParams p) {
     for (int j = 0; j < E; ++j) q_s[g * D + j * 32 + lane] = v[j] * p.scale_log2;
   }
   __syncthreads();
+  TQ_DSTAMP(3);
 
   // B fragments of the score mma: lane (r, c) holds head r (+8 nt) at dims
   // c*D/4 + 4kb + {0,1} and {2,3}, the same permutation as the K runs.
@@ -776,6 +794,7 @@ decode_mma_kernel(DecodeParams p) {
     s_fail = 1;
   }
 
+  TQ_DSTAMP(4);
   // the split-merge grid may be scheduled as CTAs reach this point
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // ---- merge the warps of this CTA through shared memory (reusing the tables) ----
@@ -827,6 +846,7 @@ decode_mma_kernel(DecodeParams p) {
     fin_l[tid] = s_fail ? 1.f : L;
   }
   __syncthreads();
+  TQ_DSTAMP(5);
   const float poison = s_fail ? __int_as_float(0x7fc00000) : 0.f;
   float* rows = fin_l + GM;  // [GM][D] normalised rows (single-split plans)
   // element i of a warp's fragment slab = (nt, mb, e, lane) -> (head, dim)
@@ -857,6 +877,7 @@ decode_mma_kernel(DecodeParams p) {
       if (p.lse && lane == 0)
         p.lse[u * G + g] = (fin_l[g] > 0.f) ? (fin_m[g] + log2f(fin_l[g])) * kLn2 : -INFINITY;
     }
+    TQ_DSTAMP(6);
     return;
   }
   if (tid < G && tid < GM) {
@@ -864,6 +885,7 @@ decode_mma_kernel(DecodeParams p) {
     dst[D] = fin_m[tid];
     dst[D + 1] = fin_l[tid];
   }
+  TQ_DSTAMP(6);
 }
 
 // Launches the tensor-core kernel for (D, BITS) (tq_decode_mma.cu).

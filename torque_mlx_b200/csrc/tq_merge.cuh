@@ -31,7 +31,10 @@ struct MergeSmem {
 // first kPrefetch o values it will weigh; the weights are formed in shared
 // memory once the row max is known, and only rows with more parts than the
 // prefetch covers go back to global memory for the rest.
-constexpr int kMergePrefetch = 16;
+// Prefetch depth: enough o values per thread that a row of up to ~80 parts
+// (a long sequence split over every SM) needs a single round trip.
+template <int SLICES>
+constexpr int merge_prefetch() { return SLICES >= 4 ? 20 : 32; }
 
 template <int D, int T>
 __device__ __forceinline__ void merge_row(const float* __restrict__ base, int nparts, float* __restrict__ out_row,
@@ -42,6 +45,7 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
   constexpr int E = D / 32;
   constexpr int NWARP = T / 32;
   constexpr int SLICES = MergeSmem<D, T>::SLICES;
+  constexpr int kMergePrefetch = merge_prefetch<SLICES>();
   float* w_s = smem;                         // [kMergeMaxParts] m_i, then the weights
   float* acc_s = w_s + kMergeMaxParts;       // [SLICES][D]
   float* red = acc_s + T;                    // [NWARP]
@@ -51,6 +55,12 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
   const int np = nparts < kMergeMaxParts ? nparts : kMergeMaxParts;
   const int dim = tid % D, slice = tid / D;
   __syncthreads();  // smem may still be in use by the caller
+  // warp 0 applies the inverse rotation at the end: its signs load now
+  float sg_a[E], sg_b[E];
+  if (inverse_rotate && warp == 0) {
+    load_signs<D>(sg_a, signs_left, lane);
+    load_signs<D>(sg_b, signs_right, lane);
+  }
 
   // 1) loads in flight together: (m, l) of parts tid, tid + T, ... and the o
   //    values of parts slice, slice + SLICES, ... (the first kPrefetch)
@@ -122,7 +132,7 @@ __device__ __forceinline__ void merge_row(const float* __restrict__ base, int np
       for (int sl = 0; sl < SLICES; ++sl) a += acc_s[sl * D + j * 32 + lane];
       v[j] = M == -INFINITY ? 0.f : a / Lsum;
     }
-    if (inverse_rotate) warp_rotate<D>(v, lane, signs_left, signs_right);
+    if (inverse_rotate) warp_rotate_regs<D>(v, lane, sg_a, sg_b);
 #pragma unroll
     for (int j = 0; j < E; ++j) out_row[j * 32 + lane] = v[j];
     if (lse_row && lane == 0) *lse_row = (M == -INFINITY) ? -INFINITY : (M + log2f(Lsum)) * kLn2;
